@@ -1,0 +1,589 @@
+// eb_api.cu -- the C ABI (include/eyebrowse_attn.h): host-side argument
+// checks, workspace sizing and kernel selection. No call allocates memory.
+#include <math.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/eyebrowse_attn.h"
+#include "eb_common.cuh"
+#include "eb_kernels.cuh"
+
+namespace eb {
+
+// Device error word: bounded waits that give up set bits here.
+__device__ unsigned g_eb_error_word;
+
+static unsigned* error_word_ptr() {
+  static unsigned* ptrs[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_eb_error_word) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<unsigned*>(p);
+  }
+  return ptrs[dev];
+}
+
+static int device_ok() {
+  static int ok_dev[64] = {};  // 0 unknown, 1 sm_100, 2 other
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!ok_dev[dev]) {
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return 0;
+    ok_dev[dev] = major == 10 ? 1 : 2;
+  }
+  return ok_dev[dev] == 1;
+}
+
+static int elem_bytes(int dt) { return dt == kF32 ? 4 : 2; }
+static bool dtype_ok(int dt) { return dt == kF32 || dt == kF16 || dt == kBF16; }
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+static constexpr float kLog2e = 1.4426950408889634f;
+static constexpr size_t kAlign = 256;
+static size_t round_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+static int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return EB_OK;
+  if (e == cudaErrorNotSupported) return EB_ERR_UNSUPPORTED;
+  cudaGetLastError();  // clear a sticky launch error
+  return EB_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------- decode plan
+struct DecodePlan {
+  int chunk, cmax;
+  size_t cnt_off, ml_off, acc_off, bytes;
+};
+
+static DecodePlan plan_decode(int64_t batch, int64_t h, int64_t hkv, int64_t hd, int dtype_cache,
+                              int64_t max_pos) {
+  DecodePlan p{};
+  const int64_t rows = max_pos + 1;
+  if (hd != 64 && hd != 128 && hd != 256) {  // SIMT path: no split
+    p.chunk = (int)rows;
+    p.cmax = 1;
+    return p;
+  }
+  const int rpb = decode_rows_per_batch((int)hd, dtype_cache);
+  const int64_t target_ctas = 2 * 148;
+  int64_t chunk = (rows * batch * hkv + target_ctas - 1) / target_ctas;
+  chunk = (chunk + rpb - 1) / rpb * rpb;
+  if (chunk < rpb) chunk = rpb;
+  if (chunk > 1024) chunk = 1024;
+  const int64_t min_chunk = (rows + 255) / 256;  // at most 256 partials per head
+  if (chunk < min_chunk) chunk = (min_chunk + rpb - 1) / rpb * rpb;
+  if (chunk >= rows) {
+    p.chunk = (int)rows;
+    p.cmax = 1;
+    return p;
+  }
+  p.chunk = (int)chunk;
+  p.cmax = (int)((rows + chunk - 1) / chunk);
+  p.cnt_off = 0;
+  p.ml_off = round_up((size_t)batch * h * sizeof(unsigned));
+  p.acc_off = p.ml_off + round_up((size_t)batch * h * p.cmax * 2 * sizeof(float));
+  p.bytes = p.acc_off + round_up((size_t)batch * h * p.cmax * hd * sizeof(float));
+  return p;
+}
+
+static bool desc_ok(const eb_attn_desc* d) {
+  if (!d) return false;
+  if (d->n_heads <= 0 || d->n_kv_heads <= 0 || d->n_heads % d->n_kv_heads) return false;
+  if (d->head_dim <= 0 || d->head_dim > 256 || (d->head_dim & 1)) return false;
+  if (d->max_seq <= 0) return false;
+  if (!dtype_ok(d->dtype_qkv) || !dtype_ok(d->dtype_cache) || !dtype_ok(d->dtype_out)) return false;
+  if (d->q_stride < 0 || d->kv_stride < 0 || d->o_stride < 0) return false;
+  return true;
+}
+static int64_t qs_of(const eb_attn_desc* d) {
+  return d->q_stride ? d->q_stride : (int64_t)d->n_heads * d->head_dim;
+}
+static int64_t kvs_of(const eb_attn_desc* d) {
+  return d->kv_stride ? d->kv_stride : (int64_t)d->n_kv_heads * d->head_dim;
+}
+static int64_t os_of(const eb_attn_desc* d) {
+  return d->o_stride ? d->o_stride : (int64_t)d->n_heads * d->head_dim;
+}
+
+// Shared body of single and batched decode.
+static int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
+                       const int32_t* positions, int64_t pos_scalar, int64_t max_pos,
+                       const void* q, const void* k, const void* v, void* kc, void* vc,
+                       int64_t cache_bstride, void* o, int64_t q_bstride, int64_t kv_bstride,
+                       int64_t o_bstride, void* ws, size_t ws_bytes, cudaStream_t st) {
+  const int hd = d->head_dim;
+  const float* cos_t = L ? L->rope_cos : nullptr;
+  const float* sin_t = L ? L->rope_sin : nullptr;
+  if ((cos_t == nullptr) != (sin_t == nullptr)) return EB_ERR_INVALID_ARGUMENT;
+  DecodePlan p = plan_decode(batch, d->n_heads, d->n_kv_heads, hd, d->dtype_cache, max_pos);
+  const bool vec = (hd == 64 || hd == 128 || hd == 256);
+  if (vec && p.cmax > 1 && (ws == nullptr || ws_bytes < p.bytes)) {
+    if (ws != nullptr && ws_bytes != 0) return EB_ERR_WORKSPACE;
+    p.chunk = (int)(max_pos + 1);  // no workspace: one CTA walks the whole context
+    p.cmax = 1;
+  }
+  if (vec) {
+    const int es = elem_bytes(d->dtype_cache);
+    if (!aligned16(kc) || !aligned16(vc) || ((cache_bstride * es) & 15)) return EB_ERR_INVALID_ARGUMENT;
+    if (p.cmax > 1 && ((reinterpret_cast<uintptr_t>(ws) & 255) != 0)) return EB_ERR_WORKSPACE;
+    DecodeArgs a{};
+    a.q = q;
+    a.k_new = k;
+    a.v_new = v;
+    a.dtype_q = d->dtype_qkv;
+    a.dtype_kv = d->dtype_qkv;
+    a.dtype_o = d->dtype_out;
+    a.q_bstride = q_bstride;
+    a.kv_bstride = kv_bstride;
+    a.o_bstride = o_bstride;
+    a.kcache = kc;
+    a.vcache = vc;
+    a.cache_bstride = cache_bstride;
+    a.o = o;
+    a.q_norm_w = L ? L->q_norm_w : nullptr;
+    a.k_norm_w = L ? L->k_norm_w : nullptr;
+    a.v_norm_w = L ? L->v_norm_w : nullptr;
+    a.cos_t = cos_t;
+    a.sin_t = sin_t;
+    a.positions = positions;
+    a.pos_scalar = (int)pos_scalar;
+    a.H = d->n_heads;
+    a.Hkv = d->n_kv_heads;
+    a.hd = hd;
+    a.chunk = p.chunk;
+    a.cmax = p.cmax;
+    a.eps = d->eps;
+    a.scale_log2 = d->scale * kLog2e;
+    if (p.cmax > 1) {
+      char* w = static_cast<char*>(ws);
+      a.ws_cnt = reinterpret_cast<unsigned*>(w + p.cnt_off);
+      a.ws_ml = reinterpret_cast<float*>(w + p.ml_off);
+      a.ws_acc = reinterpret_cast<float*>(w + p.acc_off);
+    }
+    a.err = error_word_ptr();
+    return cuda_status(launch_decode(a, d->dtype_cache, (int)batch, st));
+  }
+  // SIMT path: K/V prep writes the cache row, then attention over the cache.
+  if (k) {
+    PrepArgs pa{};
+    pa.k = k;
+    pa.v = v;
+    pa.dtype_kv = d->dtype_qkv;
+    pa.kv_stride = kvs_of(d);
+    pa.kv_bstride = kv_bstride;
+    pa.kcache = kc;
+    pa.vcache = vc;
+    pa.dtype_cache = d->dtype_cache;
+    pa.cache_bstride = cache_bstride;
+    pa.rows = 1;
+    pa.hkv = d->n_kv_heads;
+    pa.hd = hd;
+    pa.pos0 = (int)pos_scalar;
+    pa.positions = positions;
+    pa.k_norm_w = L ? L->k_norm_w : nullptr;
+    pa.v_norm_w = L ? L->v_norm_w : nullptr;
+    pa.cos_t = cos_t;
+    pa.sin_t = sin_t;
+    pa.eps = d->eps;
+    pa.batch = (int)batch;
+    cudaError_t e = launch_prep_kv(pa, st);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  SimtArgs s{};
+  s.q = q;
+  s.dtype_q = d->dtype_qkv;
+  s.q_stride = 0;
+  s.q_bstride = q_bstride;
+  s.k = kc;
+  s.v = vc;
+  s.dtype_kv = d->dtype_cache;
+  s.kv_stride = (int64_t)d->n_kv_heads * hd;
+  s.kv_bstride = cache_bstride;
+  s.o = o;
+  s.dtype_o = d->dtype_out;
+  s.o_stride = 0;
+  s.o_bstride = o_bstride;
+  s.rows = 1;
+  s.H = d->n_heads;
+  s.Hkv = d->n_kv_heads;
+  s.hd = hd;
+  s.qpos0 = (int)pos_scalar;
+  s.positions = positions;
+  s.q_norm_w = L ? L->q_norm_w : nullptr;
+  s.cos_t = cos_t;
+  s.sin_t = sin_t;
+  s.eps = d->eps;
+  s.scale = d->scale;
+  s.batch = (int)batch;
+  return cuda_status(launch_attn_simt(s, st));
+}
+
+}  // namespace eb
+
+using namespace eb;
+
+extern "C" {
+
+const char* eb_status_string(int status) {
+  switch (status) {
+    case EB_OK: return "ok";
+    case EB_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case EB_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case EB_ERR_CUDA: return "CUDA error";
+    case EB_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case EB_ERR_NO_DEVICE: return "no sm_100 device";
+    case EB_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait timed out";
+  }
+  return "unknown status";
+}
+
+const char* eb_version(void) { return "eyebrowse-b200 0.1 (sm_100a)"; }
+
+// ---------------------------------------------------------------- kernel-level
+size_t eb_attn_prefill_workspace_bytes(int64_t h, int64_t hkv, int64_t s, int64_t hd) {
+  (void)h;
+  if (!prefill_tc_supported((int)hd) || s <= 0 || hkv <= 0) return 0;
+  return round_up((size_t)4 * s * hkv * hd * sizeof(__half));
+}
+
+int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, int64_t h,
+                    int64_t hkv, int64_t s, int64_t hd, float scale, void* workspace,
+                    size_t workspace_bytes, eb_stream_t stream) {
+  if (h <= 0 || hkv <= 0 || h % hkv || hd <= 0 || hd > 256 || (hd & 1) || s < 0)
+    return EB_ERR_INVALID_ARGUMENT;
+  if (s == 0) return EB_OK;
+  if (!q || !k || !v || !o) return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (prefill_tc_supported((int)hd)) {
+    const size_t need = eb_attn_prefill_workspace_bytes(h, hkv, s, hd);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace)) return EB_ERR_WORKSPACE;
+    if (!aligned16(q) || !aligned16(o)) return EB_ERR_INVALID_ARGUMENT;
+    PrepArgs pa{};
+    pa.k = k;
+    pa.v = v;
+    pa.dtype_kv = kF32;
+    pa.kv_stride = hkv * hd;
+    pa.dtype_cache = kF32;
+    pa.split = workspace;
+    pa.rows = (int)s;
+    pa.hkv = (int)hkv;
+    pa.hd = (int)hd;
+    pa.batch = 1;
+    cudaError_t e = launch_prep_kv(pa, st);
+    if (e != cudaSuccess) return cuda_status(e);
+    PrefillArgs a{};
+    a.q = q;
+    a.dtype_q = kF32;
+    a.q_stride = h * hd;
+    a.o = o;
+    a.dtype_o = kF32;
+    a.o_stride = h * hd;
+    a.S = (int)s;
+    a.H = (int)h;
+    a.Hkv = (int)hkv;
+    a.scale_log2 = scale * kLog2e;
+    a.err = error_word_ptr();
+    if (!a.err) return EB_ERR_CUDA;
+    return cuda_status(launch_prefill_tc(a, (int)hd, nullptr, nullptr, false, workspace, st));
+  }
+  SimtArgs sa{};
+  sa.q = q;
+  sa.dtype_q = kF32;
+  sa.q_stride = h * hd;
+  sa.k = k;
+  sa.v = v;
+  sa.dtype_kv = kF32;
+  sa.kv_stride = hkv * hd;
+  sa.o = o;
+  sa.dtype_o = kF32;
+  sa.o_stride = h * hd;
+  sa.rows = (int)s;
+  sa.H = (int)h;
+  sa.Hkv = (int)hkv;
+  sa.hd = (int)hd;
+  sa.scale = scale;
+  sa.batch = 1;
+  return cuda_status(launch_attn_simt(sa, st));
+}
+
+size_t eb_attn_decode_workspace_bytes(int64_t h, int64_t hkv, int64_t pos, int64_t hd) {
+  if (h <= 0 || hkv <= 0 || pos < 0) return 0;
+  return plan_decode(1, h, hkv, hd, kF32, pos).bytes;
+}
+
+int eb_attn_decode(const float* q, const float* kcache, const float* vcache, float* o, int64_t h,
+                   int64_t hkv, int64_t pos, int64_t hd, int64_t max_seq, float scale,
+                   void* workspace, size_t workspace_bytes, eb_stream_t stream) {
+  if (h <= 0 || hkv <= 0 || h % hkv || hd <= 0 || hd > 256 || (hd & 1) || pos < 0 ||
+      pos >= max_seq)
+    return EB_ERR_INVALID_ARGUMENT;
+  if (!q || !kcache || !vcache || !o) return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  eb_attn_desc d{};
+  d.n_heads = (int32_t)h;
+  d.n_kv_heads = (int32_t)hkv;
+  d.head_dim = (int32_t)hd;
+  d.max_seq = (int32_t)max_seq;
+  d.dtype_qkv = EB_F32;
+  d.dtype_cache = EB_F32;
+  d.dtype_out = EB_F32;
+  d.scale = scale;
+  return decode_impl(&d, nullptr, 1, nullptr, pos, pos, q, nullptr, nullptr,
+                     const_cast<float*>(kcache), const_cast<float*>(vcache), 0, o, 0, 0, 0,
+                     workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int eb_rope(const float* x, const float* cos_t, const float* sin_t, float* out, int64_t seq,
+            int64_t n_heads, int64_t head_dim, int64_t base_pos, eb_stream_t stream) {
+  if (seq < 0 || n_heads <= 0 || head_dim <= 0 || (head_dim & 1) || base_pos < 0)
+    return EB_ERR_INVALID_ARGUMENT;
+  if (seq == 0) return EB_OK;
+  if (!x || !cos_t || !sin_t || !out) return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  return cuda_status(launch_rope(x, cos_t, sin_t, out, seq, n_heads, head_dim, base_pos,
+                                 reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int eb_kv_write(float* cache, const float* src, int64_t hkv, int64_t count, int64_t hd,
+                int64_t max_seq, int64_t dst_start, eb_stream_t stream) {
+  if (hkv <= 0 || count < 0 || hd <= 0 || dst_start < 0 || dst_start + count > max_seq)
+    return EB_ERR_INVALID_ARGUMENT;
+  if (count == 0) return EB_OK;
+  if (!cache || !src) return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  return cuda_status(launch_kv_write(cache, src, hkv, count, hd, dst_start,
+                                     reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int eb_rmsnorm(const float* x, const float* weight, float* out, int64_t rows, int64_t dim,
+               float eps, eb_stream_t stream) {
+  if (rows < 0 || dim <= 0) return EB_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return EB_OK;
+  if (!x || !weight || !out) return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  return cuda_status(
+      launch_rmsnorm(x, weight, out, rows, dim, eps, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int eb_rope_tables(float* cos_t, float* sin_t, int64_t max_seq, int64_t head_dim,
+                   int64_t rope_angles, float theta) {
+  // crates/eyebrowse-nn/src/rope.rs:24-50: f64 angles, cast to f32; pairs past
+  // rope_angles keep cos = 1, sin = 0.
+  if (!cos_t || !sin_t || max_seq < 0 || head_dim <= 0 || (head_dim & 1) || rope_angles < 0)
+    return EB_ERR_INVALID_ARGUMENT;
+  const int64_t half = head_dim / 2;
+  for (int64_t i = 0; i < max_seq * half; i++) {
+    cos_t[i] = 1.0f;
+    sin_t[i] = 0.0f;
+  }
+  const double th = (double)theta, hdd = (double)head_dim;
+  const int64_t n = rope_angles < half ? rope_angles : half;
+  for (int64_t s = 0; s < max_seq; s++)
+    for (int64_t k = 0; k < n; k++) {
+      const double inv_freq = pow(th, -(2.0 * (double)k) / hdd);
+      const double angle = (double)s * inv_freq;
+      cos_t[s * half + k] = (float)cos(angle);
+      sin_t[s * half + k] = (float)sin(angle);
+    }
+  return EB_OK;
+}
+
+// ---------------------------------------------------------------- fused primitive
+size_t eb_attention_prefill_workspace_bytes(const eb_attn_desc* d, int64_t seq) {
+  if (!desc_ok(d) || seq <= 0) return 0;
+  if (!prefill_tc_supported(d->head_dim) || d->dtype_cache != EB_F32) return 0;
+  return round_up((size_t)4 * seq * d->n_kv_heads * d->head_dim * sizeof(__half));
+}
+
+// Shared argument checks of the prefill entry points.
+static int prefill_check(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq, void* ws,
+                         size_t ws_bytes) {
+  if (!desc_ok(d) || seq < 0 || seq > d->max_seq) return EB_ERR_INVALID_ARGUMENT;
+  const float* cos_t = L ? L->rope_cos : nullptr;
+  const float* sin_t = L ? L->rope_sin : nullptr;
+  if ((cos_t == nullptr) != (sin_t == nullptr)) return EB_ERR_INVALID_ARGUMENT;
+  if (seq == 0) return EB_OK;
+  if (prefill_tc_supported(d->head_dim) && d->dtype_cache == EB_F32) {
+    const size_t need = eb_attention_prefill_workspace_bytes(d, seq);
+    if (!ws || ws_bytes < need || !aligned16(ws)) return EB_ERR_WORKSPACE;
+  }
+  return EB_OK;
+}
+
+int eb_attention_prefill_kv(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq,
+                            const void* k, const void* v, void* kcache, void* vcache,
+                            void* workspace, size_t workspace_bytes, eb_stream_t stream) {
+  int rc = prefill_check(d, L, seq, workspace, workspace_bytes);
+  if (rc != EB_OK || seq == 0) return rc;
+  if (!k || !v || !kcache || !vcache) return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  const bool split = prefill_tc_supported(d->head_dim) && d->dtype_cache == EB_F32;
+  PrepArgs pa{};
+  pa.k = k;
+  pa.v = v;
+  pa.dtype_kv = d->dtype_qkv;
+  pa.kv_stride = kvs_of(d);
+  pa.kcache = kcache;
+  pa.vcache = vcache;
+  pa.dtype_cache = d->dtype_cache;
+  pa.split = split ? workspace : nullptr;
+  pa.rows = (int)seq;
+  pa.hkv = d->n_kv_heads;
+  pa.hd = d->head_dim;
+  pa.k_norm_w = L ? L->k_norm_w : nullptr;
+  pa.v_norm_w = L ? L->v_norm_w : nullptr;
+  pa.cos_t = L ? L->rope_cos : nullptr;
+  pa.sin_t = L ? L->rope_sin : nullptr;
+  pa.eps = d->eps;
+  pa.batch = 1;
+  return cuda_status(launch_prep_kv(pa, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int eb_attention_prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq,
+                                const void* q, const void* kcache, const void* vcache, void* o,
+                                void* workspace, size_t workspace_bytes, eb_stream_t stream) {
+  int rc = prefill_check(d, L, seq, workspace, workspace_bytes);
+  if (rc != EB_OK || seq == 0) return rc;
+  if (!q || !kcache || !vcache || !o) return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int hd = d->head_dim;
+  const float* cos_t = L ? L->rope_cos : nullptr;
+  const float* sin_t = L ? L->rope_sin : nullptr;
+  if (prefill_tc_supported(hd)) {
+    const bool split = d->dtype_cache == EB_F32;
+    const int eq = elem_bytes(d->dtype_qkv), eo = elem_bytes(d->dtype_out);
+    if (!aligned16(q) || !aligned16(o) || !aligned16(kcache) || !aligned16(vcache) ||
+        ((qs_of(d) * eq) & 15) || ((os_of(d) * eo) & 15))
+      return EB_ERR_INVALID_ARGUMENT;
+    PrefillArgs a{};
+    a.q = q;
+    a.dtype_q = d->dtype_qkv;
+    a.q_stride = qs_of(d);
+    a.q_norm_w = L ? L->q_norm_w : nullptr;
+    a.cos_t = cos_t;
+    a.sin_t = sin_t;
+    a.eps = d->eps;
+    a.o = o;
+    a.dtype_o = d->dtype_out;
+    a.o_stride = os_of(d);
+    a.S = (int)seq;
+    a.H = d->n_heads;
+    a.Hkv = d->n_kv_heads;
+    a.scale_log2 = d->scale * kLog2e;
+    a.err = error_word_ptr();
+    if (!a.err) return EB_ERR_CUDA;
+    return cuda_status(launch_prefill_tc(a, hd, kcache, vcache, d->dtype_cache == EB_BF16,
+                                         split ? workspace : nullptr, st));
+  }
+  SimtArgs s{};
+  s.q = q;
+  s.dtype_q = d->dtype_qkv;
+  s.q_stride = qs_of(d);
+  s.k = kcache;
+  s.v = vcache;
+  s.dtype_kv = d->dtype_cache;
+  s.kv_stride = (int64_t)d->n_kv_heads * hd;
+  s.o = o;
+  s.dtype_o = d->dtype_out;
+  s.o_stride = os_of(d);
+  s.rows = (int)seq;
+  s.H = d->n_heads;
+  s.Hkv = d->n_kv_heads;
+  s.hd = hd;
+  s.q_norm_w = L ? L->q_norm_w : nullptr;
+  s.cos_t = cos_t;
+  s.sin_t = sin_t;
+  s.eps = d->eps;
+  s.scale = d->scale;
+  s.batch = 1;
+  return cuda_status(launch_attn_simt(s, st));
+}
+
+int eb_attention_prefill(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq,
+                         const void* q, const void* k, const void* v, void* kcache,
+                         void* vcache, void* o, void* workspace, size_t workspace_bytes,
+                         eb_stream_t stream) {
+  int rc = prefill_check(d, L, seq, workspace, workspace_bytes);
+  if (rc != EB_OK || seq == 0) return rc;
+  if (!q || !o) return EB_ERR_INVALID_ARGUMENT;
+  rc = eb_attention_prefill_kv(d, L, seq, k, v, kcache, vcache, workspace, workspace_bytes,
+                               stream);
+  if (rc != EB_OK) return rc;
+  return eb_attention_prefill_attend(d, L, seq, q, kcache, vcache, o, workspace, workspace_bytes,
+                                     stream);
+}
+
+size_t eb_attention_decode_workspace_bytes(const eb_attn_desc* d, int64_t batch,
+                                           int64_t max_pos) {
+  if (!desc_ok(d) || batch <= 0 || max_pos < 0) return 0;
+  return plan_decode(batch, d->n_heads, d->n_kv_heads, d->head_dim, d->dtype_cache, max_pos).bytes;
+}
+
+int eb_attention_decode(const eb_attn_desc* d, const eb_attn_layer* L, int64_t pos,
+                        const void* q, const void* k, const void* v, void* kcache, void* vcache,
+                        void* o, void* workspace, size_t workspace_bytes, eb_stream_t stream) {
+  if (!desc_ok(d) || pos < 0 || pos >= d->max_seq) return EB_ERR_INVALID_ARGUMENT;
+  if (!q || !k || !v || !kcache || !vcache || !o) return EB_ERR_INVALID_ARGUMENT;
+  if (d->q_stride || d->kv_stride || d->o_stride) return EB_ERR_UNSUPPORTED;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  return decode_impl(d, L, 1, nullptr, pos, pos, q, k, v, kcache, vcache, 0, o, 0, 0, 0,
+                     workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int eb_attention_decode_batched(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
+                                const int32_t* positions, int64_t max_pos, const void* q,
+                                const void* k, const void* v, void* kcache, void* vcache,
+                                int64_t cache_batch_stride, void* o, void* workspace,
+                                size_t workspace_bytes, eb_stream_t stream) {
+  if (!desc_ok(d) || batch < 0 || max_pos < 0 || max_pos >= d->max_seq)
+    return EB_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return EB_OK;
+  if (!positions || !q || !k || !v || !kcache || !vcache || !o) return EB_ERR_INVALID_ARGUMENT;
+  if (d->q_stride || d->kv_stride || d->o_stride) return EB_ERR_UNSUPPORTED;
+  if (cache_batch_stride < (int64_t)d->max_seq * d->n_kv_heads * d->head_dim)
+    return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  const int64_t hq = (int64_t)d->n_heads * d->head_dim;
+  const int64_t hk = (int64_t)d->n_kv_heads * d->head_dim;
+  return decode_impl(d, L, batch, positions, 0, max_pos, q, k, v, kcache, vcache,
+                     cache_batch_stride, o, hq, hk, hq, workspace, workspace_bytes,
+                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+int eb_workspace_init(void* workspace, size_t workspace_bytes, eb_stream_t stream) {
+  if (!workspace || workspace_bytes == 0) return EB_OK;
+  return cuda_status(cudaMemsetAsync(workspace, 0, workspace_bytes,
+                                     reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int eb_head_concat(const void* src, void* dst, int64_t shards, int64_t rows, int64_t heads_per,
+                   int64_t head_dim, int32_t dtype, eb_stream_t stream) {
+  if (!src || !dst || shards <= 0 || rows < 0 || heads_per <= 0 || head_dim <= 0 || !dtype_ok(dtype))
+    return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  return cuda_status(launch_head_concat(src, dst, shards, rows, heads_per, head_dim,
+                                        elem_bytes(dtype), reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int eb_get_device_error(uint32_t* bits) {
+  if (!bits) return EB_ERR_INVALID_ARGUMENT;
+  unsigned* p = error_word_ptr();
+  if (!p) return EB_ERR_CUDA;
+  unsigned v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return EB_ERR_CUDA;
+  if (cudaMemcpy(&v, p, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return EB_ERR_CUDA;
+  const unsigned zero = 0;
+  if (cudaMemcpy(p, &zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess) return EB_ERR_CUDA;
+  *bits = v;
+  return v ? EB_ERR_DEVICE_TIMEOUT : EB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,127 @@
+// eb_kernels.cuh -- argument blocks and launchers shared between the kernel
+// translation units and the C-ABI layer (eb_api.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace eb {
+
+// ------------------------------------------------------------- small kernels
+cudaError_t launch_rope(const float* x, const float* cos_t, const float* sin_t, float* out,
+                        int64_t seq, int64_t n_heads, int64_t hd, int64_t base_pos,
+                        cudaStream_t st);
+cudaError_t launch_kv_write(float* cache, const float* src, int64_t hkv, int64_t count, int64_t hd,
+                            int64_t dst_start, cudaStream_t st);
+cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int64_t rows, int64_t dim,
+                           float eps, cudaStream_t st);
+cudaError_t launch_head_concat(const void* src, void* dst, int64_t shards, int64_t rows,
+                               int64_t heads_per, int64_t hd, int elem_bytes, cudaStream_t st);
+
+// K/V preparation for a run of rows: k -> RMSNorm(k_norm_w) -> RoPE(row pos0+r),
+// v -> RMSNorm(v_norm_w); written to the cache rows [dst0, dst0+rows) in the
+// cache dtype, and (split != nullptr) as f16 hi/lo planes for the tensor-core
+// path: split = [khi | klo | vhi | vlo], each rows*hkv*hd halves, of the values
+// as stored (cache-rounded). batch > 1 handles `batch` sequences, each with
+// its own position (positions[b]) and cache (cache + b*cache_bstride).
+struct PrepArgs {
+  const void* k;
+  const void* v;
+  int dtype_kv;
+  int64_t kv_stride;   // elements between rows of k/v
+  int64_t kv_bstride;  // elements between sequences of k/v
+  void* kcache;
+  void* vcache;
+  int dtype_cache;
+  int64_t cache_bstride;
+  void* split;         // f16 planes or nullptr
+  int rows, hkv, hd;
+  int pos0;                  // position of row 0 (prefill 0)
+  const int32_t* positions;  // per-sequence position (overrides pos0) or nullptr
+  const float* k_norm_w;
+  const float* v_norm_w;
+  const float* cos_t;
+  const float* sin_t;
+  float eps;
+  int batch;
+};
+cudaError_t launch_prep_kv(const PrepArgs& a, cudaStream_t st);
+
+// Generic SIMT attention (any even head_dim <= 256): one warp per (query row,
+// query head); the q row is normalised/rotated inline. Query row i of
+// sequence b has position qpos0 + i (or positions[b] for decode), attends
+// key rows 0..=that position of k/v.
+struct SimtArgs {
+  const void* q;
+  int dtype_q;
+  int64_t q_stride, q_bstride;
+  const void* k;
+  const void* v;
+  int dtype_kv;
+  int64_t kv_stride, kv_bstride;
+  void* o;
+  int dtype_o;
+  int64_t o_stride, o_bstride;
+  int rows, H, Hkv, hd;
+  int qpos0;
+  const int32_t* positions;
+  const float* q_norm_w;
+  const float* cos_t;
+  const float* sin_t;
+  float eps, scale;
+  int batch;
+};
+cudaError_t launch_attn_simt(const SimtArgs& a, cudaStream_t st);
+
+// ------------------------------------------------------------- decode
+struct DecodeArgs {
+  const void* q;       // [B][H][hd] (row = head), dtype_q
+  const void* k_new;   // [B][Hkv][hd] or nullptr (no cache write)
+  const void* v_new;
+  int dtype_q, dtype_kv, dtype_o;
+  int64_t q_bstride, kv_bstride, o_bstride;  // elements between sequences
+  void* kcache;
+  void* vcache;
+  int64_t cache_bstride;
+  void* o;
+  const float* q_norm_w;
+  const float* k_norm_w;
+  const float* v_norm_w;
+  const float* cos_t;
+  const float* sin_t;
+  const int32_t* positions;  // device, per sequence; nullptr -> pos_scalar
+  int pos_scalar;
+  int H, Hkv, hd, chunk, cmax;
+  float eps, scale_log2;
+  float* ws_ml;        // [B][H][cmax] x (m, l)
+  float* ws_acc;       // [B][H][cmax][hd]
+  unsigned* ws_cnt;    // [B][Hkv] tickets
+  unsigned* err;
+};
+// Returns cudaErrorNotSupported when (hd, cache dtype) has no vector kernel.
+cudaError_t launch_decode(const DecodeArgs& a, int dtype_cache, int batch, cudaStream_t st);
+int decode_rows_per_batch(int hd, int dtype_cache);
+
+// ------------------------------------------------------------- prefill (tcgen05)
+struct PrefillArgs {
+  const void* q;
+  int dtype_q;
+  int64_t q_stride;
+  const float* q_norm_w;
+  const float* cos_t;
+  const float* sin_t;
+  float eps;
+  void* o;
+  int dtype_o;
+  int64_t o_stride;
+  int S, H, Hkv;
+  float scale_log2;
+  unsigned* err;
+};
+// kv16: 16-bit K/V rows [S][Hkv][hd] the tensor cores read (the cache when it
+// is f16/bf16). split: f16 hi/lo planes when the inputs are f32 (kv16 unused).
+cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* k16, const void* v16,
+                              bool bf16, const void* split, cudaStream_t st);
+bool prefill_tc_supported(int hd);
+
+}  // namespace eb

@@ -1,0 +1,579 @@
+// eb_prefill.cu -- causal GQA flash-attention prefill on tcgen05 tensor cores.
+//
+// Replaces attn_prefill (crates/eyebrowse-kernels/src/attention.rs:10-50,
+// :94-120): o[i,h] = softmax_j<=i(scale * q[i,h] . k[j,kvh]) v[j,kvh], with
+// kvh = h / (H/Hkv), seq-major layouts.
+//
+// One CTA = one 128-row query tile of one query head (256 threads):
+//   warp 0      TMA producer: K/V tiles [BN rows x 64 dims] (128-byte swizzle)
+//               into an NST-deep shared-memory ring.
+//   warp 1      TMEM owner + MMA issuer (one thread): S = Q K^T into TMEM,
+//               then O += P V into TMEM.
+//   warps 4..7  one thread per query row: load the q row, RMSNorm + RoPE it
+//               in registers, write it as the swizzled MMA operand; per KV
+//               tile read the S row from TMEM, online softmax in f32 (exp2),
+//               rescale the O row in TMEM when the max moves, write P (16-bit)
+//               as the operand of the PV MMA; finally O / l to global memory.
+// K/V come from the cache the K/V preparation pass has just written (the
+// reference attends the same post-RoPE k / post-norm v it writes,
+// crates/eyebrowse-nn/src/attention.rs:78-115).
+//
+// f32 inputs (SPLIT): every operand x is carried as two f16 values
+// hi = f16(x), lo = f16(x - hi); S = Qh.Kh + Qh.Kl + Ql.Kh and
+// O += Ph.Vh + Ph.Vl + Pl.Vh (the standard error-compensated split, which
+// keeps ~21 mantissa bits on f16 tensor cores).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "eb_common.cuh"
+#include "eb_kernels.cuh"
+#include "eb_rowops.cuh"
+
+namespace eb {
+
+constexpr int constexpr_pow2ceil(int x) {
+  int p = 32;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+template <int HD, int BN, bool SPLIT, int NST>
+struct PfCfg {
+  static constexpr int NQP = SPLIT ? 2 : 1;  // operand planes (hi, lo)
+  static constexpr int HB = HD / 64;         // 64-element boxes along head_dim
+  static constexpr int PB = BN >= 64 ? BN / 64 : 1;
+  static constexpr int TILE128 = 128 * 128;  // one [128 rows x 128 B] box
+  static constexpr int Q_BYTES = NQP * HB * TILE128;
+  static constexpr int P_BYTES = NQP * PB * TILE128;
+  static constexpr int KV_BOX = BN * 128;  // one [BN rows x 128 B] box
+  static constexpr int K_BYTES = NQP * HB * KV_BOX;
+  static constexpr int STAGE_BYTES = 2 * K_BYTES;
+  static constexpr int BAR_OFF = Q_BYTES + P_BYTES + NST * STAGE_BYTES;
+  static constexpr int SMEM = BAR_OFF + 512 + 1024;  // barriers/flags + alignment slack
+  static constexpr int TMEM_COLS = constexpr_pow2ceil(HD + BN);
+  static constexpr uint32_t O_COL = 0, S_COL = HD;
+  static_assert(HD % 64 == 0 && HD <= 256, "head_dim");
+  static_assert(BN % 32 == 0 && BN <= 128, "kv tile");
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+// Barrier slots in the barrier area.
+enum { kBarQ = 0, kBarSFull, kBarSFree, kBarPFull, kBarODone, kBarFinal, kBarKV };
+
+__device__ __forceinline__ void load8_any(const void* p, int64_t idx, int dt, float (&f)[8]) {
+  if (dt == kF32) {
+    const float4* v = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + idx);
+    const float4 a = v[0], b = v[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else if (dt == kF16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p) + idx);
+    const __half* h = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; i++) f[i] = __half2float(h[i]);
+  } else {
+    const uint4 u =
+        *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p) + idx);
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int i = 0; i < 8; i++) f[i] = __bfloat162float(h[i]);
+  }
+}
+
+// 8 floats -> one 16-byte chunk of 16-bit operands at a shared address.
+template <bool BF16>
+__device__ __forceinline__ void st_chunk(uint32_t saddr, const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+    w[i] = BF16 ? pack_bf162(f[2 * i], f[2 * i + 1]) : pack_half2(f[2 * i], f[2 * i + 1]);
+  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(saddr), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3])
+               : "memory");
+}
+// hi / lo split of 8 floats into two chunks.
+__device__ __forceinline__ void st_chunk_split(uint32_t s_hi, uint32_t s_lo, const float (&f)[8]) {
+  float hi[8], lo[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    hi[i] = __half2float(__float2half_rn(f[i]));
+    lo[i] = f[i] - hi[i];
+  }
+  st_chunk<false>(s_hi, hi);
+  st_chunk<false>(s_lo, lo);
+}
+
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, unsigned* err,
+                                           unsigned bit) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (;;) {
+    for (int i = 0; i < 32; i++)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      atomicOr(err, bit);
+      return false;
+    }
+  }
+}
+
+template <int HD, int BN, bool SPLIT, bool BF16, int NST>
+__global__ void __launch_bounds__(256, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV,
+                      const __grid_constant__ CUtensorMap tmKlo,
+                      const __grid_constant__ CUtensorMap tmVlo, PrefillArgs a) {
+  using C = PfCfg<HD, BN, SPLIT, NST>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sP = sQ + C::Q_BYTES;
+  const uint32_t sKV = sP + C::P_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::BAR_OFF + 384);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::BAR_OFF + 392);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int kKFull0 = kBarKV, kKEmpty0 = kBarKV + NST, kVFull0 = kBarKV + 2 * NST,
+            kVEmpty0 = kBarKV + 3 * NST;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (a.S + 127) / 128;
+  const int qt = n_qt - 1 - (int)(blockIdx.x / a.H);  // longest causal rows first
+  const int h = (int)(blockIdx.x % a.H);
+  const int kvh = h / (a.H / a.Hkv);
+  const int q0 = qt * 128;
+  const int kv_rows = min(q0 + 128, a.S);
+  const int n_tiles = (kv_rows + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(kBarQ), 128);
+    mbar_init(bar(kBarSFull), 1);
+    mbar_init(bar(kBarSFree), 128);
+    mbar_init(bar(kBarPFull), 128);
+    mbar_init(bar(kBarODone), 1);
+    mbar_init(bar(kBarFinal), 1);
+    for (int s = 0; s < 4 * NST; s++) mbar_init(bar(kBarKV + s), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmK);
+    tma_prefetch_map(&tmV);
+    if (SPLIT) {
+      tma_prefetch_map(&tmKlo);
+      tma_prefetch_map(&tmVlo);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    // K tile j and V tile j use ring slot j % NST; K is released when QK_j
+    // completes, V when PV_j completes, so K_{j+1} streams in under PV_j.
+    if (lane == 0) {
+      int kiss[NST], viss[NST];
+      for (int s = 0; s < NST; s++) kiss[s] = viss[s] = 0;
+      for (int j = 0; j < n_tiles; j++) {
+        const int st = j % NST;
+        const uint32_t kst = sKV + st * C::STAGE_BYTES;
+        const uint32_t vst = kst + C::K_BYTES;
+        if (j >= NST &&
+            !mbar_wait(bar(kKEmpty0 + st), (j / NST - 1) & 1, abort_flag, a.err, kErrTimeoutTma))
+          break;
+        const uint32_t kf = bar(kKFull0 + st);
+        mbar_arrive_expect_tx(kf, C::K_BYTES);
+#pragma unroll
+        for (int hb = 0; hb < C::HB; hb++) {
+          tma_load_3d(kst + hb * C::KV_BOX, &tmK, kf, hb * 64, kvh, j * BN);
+          if (SPLIT) tma_load_3d(kst + (C::HB + hb) * C::KV_BOX, &tmKlo, kf, hb * 64, kvh, j * BN);
+        }
+        kiss[st]++;
+        if (j >= NST &&
+            !mbar_wait(bar(kVEmpty0 + st), (j / NST - 1) & 1, abort_flag, a.err, kErrTimeoutTma))
+          break;
+        const uint32_t vf = bar(kVFull0 + st);
+        mbar_arrive_expect_tx(vf, C::K_BYTES);
+#pragma unroll
+        for (int hb = 0; hb < C::HB; hb++) {
+          tma_load_3d(vst + hb * C::KV_BOX, &tmV, vf, hb * 64, kvh, j * BN);
+          if (SPLIT) tma_load_3d(vst + (C::HB + hb) * C::KV_BOX, &tmVlo, vf, hb * 64, kvh, j * BN);
+        }
+        viss[st]++;
+      }
+      // Every issued copy has landed before the CTA can exit.
+      for (int s = 0; s < NST; s++) {
+        if (kiss[s]) mbar_drain(bar(kKFull0 + s), (kiss[s] - 1) & 1, a.err, kErrTimeoutTma);
+        if (viss[s]) mbar_drain(bar(kVFull0 + s), (viss[s] - 1) & 1, a.err, kErrTimeoutTma);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    // Order per tile j: QK_j (overlaps the softmax of tile j-1), then
+    // PV_{j-1} once P_{j-1} is written.
+    if (lane == 0) {
+      const uint32_t tS = tmem + C::S_COL, tO = tmem + C::O_COL;
+      constexpr uint32_t idesc_qk = idesc_f16(128, BN, BF16, false);
+      constexpr uint32_t idesc_pv = idesc_f16(128, HD, BF16, true);
+      auto issue_qk = [&](int st) {
+        const uint32_t kst = sKV + st * C::STAGE_BYTES;
+        constexpr int NPASS = SPLIT ? 3 : 1;
+#pragma unroll
+        for (int pass = 0; pass < NPASS; pass++) {
+          const int qa = (pass == 2) ? 1 : 0;  // Qh Kh, Qh Kl, Ql Kh
+          const int kb = (pass == 1) ? 1 : 0;
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; kk++) {
+            const int hb = kk >> 2, w = kk & 3;
+            const uint64_t ad =
+                sdesc_sw128(sQ + (qa * C::HB + hb) * C::TILE128 + w * 32, 16, 1024);
+            const uint64_t bd =
+                sdesc_sw128(kst + (kb * C::HB + hb) * C::KV_BOX + w * 32, 16, 1024);
+            umma_ss(tS, ad, bd, idesc_qk, (pass > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+      };
+      auto issue_pv = [&](int st, bool first) {
+        const uint32_t vst = sKV + st * C::STAGE_BYTES + C::K_BYTES;
+        constexpr int NPASS = SPLIT ? 3 : 1;
+#pragma unroll
+        for (int pass = 0; pass < NPASS; pass++) {
+          const int pa = (pass == 2) ? 1 : 0;  // Ph Vh, Ph Vl, Pl Vh
+          const int vb = (pass == 1) ? 1 : 0;
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; kk++) {
+            const int pb = kk >> 2, w = kk & 3;
+            const uint64_t ad =
+                sdesc_sw128(sP + (pa * C::PB + pb) * C::TILE128 + w * 32, 16, 1024);
+            const uint64_t bd =
+                sdesc_sw128(vst + vb * C::HB * C::KV_BOX + kk * 16 * 128, C::KV_BOX, 1024);
+            umma_ss(tO, ad, bd, idesc_pv, (!first || pass > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+      };
+      auto pv_step = [&](int t) -> bool {  // PV for tile t
+        const int pst = t % NST;
+        if (!mbar_wait(bar(kBarPFull), t & 1, abort_flag, a.err, kErrTimeoutMma)) return false;
+        if (!mbar_wait(bar(kVFull0 + pst), (t / NST) & 1, abort_flag, a.err, kErrTimeoutMma))
+          return false;
+        tc_fence_after();
+        issue_pv(pst, t == 0);
+        umma_commit(bar(kBarODone));
+        umma_commit(bar(kVEmpty0 + pst));
+        return true;
+      };
+      bool ok = mbar_wait(bar(kBarQ), 0, abort_flag, a.err, kErrTimeoutMma);
+      tc_fence_after();
+      for (int j = 0; ok && j < n_tiles; j++) {
+        const int st = j % NST;
+        if (!mbar_wait(bar(kKFull0 + st), (j / NST) & 1, abort_flag, a.err, kErrTimeoutMma)) break;
+        if (j > 0 && !mbar_wait(bar(kBarSFree), (j - 1) & 1, abort_flag, a.err, kErrTimeoutMma))
+          break;
+        tc_fence_after();
+        issue_qk(st);
+        umma_commit(bar(kBarSFull));
+        umma_commit(bar(kKEmpty0 + st));
+        if (j > 0 && !pv_step(j - 1)) break;
+        if (j == n_tiles - 1 && !pv_step(j)) break;
+      }
+      // Every issued MMA has completed before TMEM is released.
+      umma_commit(bar(kBarFinal));
+      mbar_drain(bar(kBarFinal), 0, a.err, kErrTimeoutMma);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax rows
+    const int r = threadIdx.x - 128;  // tile row == TMEM lane
+    const int q_row = q0 + r;
+    const bool valid = q_row < a.S;
+    const uint32_t trow = tmem + ((uint32_t)((warp - 4) * 32) << 16);
+    // Q row: RMSNorm (pass 1: sum of squares), then norm + RoPE per 8-wide
+    // chunk pair (p, p + HD/2) straight into the swizzled operand.
+    {
+      const int64_t qbase = (int64_t)q_row * a.q_stride + (int64_t)h * HD;
+      float inv = 1.f;
+      if (valid && a.q_norm_w) {
+        float ss = 0.f;
+        for (int d = 0; d < HD; d += 8) {
+          float f[8];
+          load8_any(a.q, qbase + d, a.dtype_q, f);
+#pragma unroll
+          for (int i = 0; i < 8; i++) ss = __fadd_rn(ss, __fmul_rn(f[i], f[i]));
+        }
+        inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+      }
+      const float* crow = a.cos_t ? a.cos_t + (int64_t)q_row * (HD / 2) : nullptr;
+      const float* srow = a.sin_t ? a.sin_t + (int64_t)q_row * (HD / 2) : nullptr;
+      for (int p0 = 0; p0 < HD / 2; p0 += 8) {
+        float x1[8], x2[8];
+        if (valid) {
+          load8_any(a.q, qbase + p0, a.dtype_q, x1);
+          load8_any(a.q, qbase + HD / 2 + p0, a.dtype_q, x2);
+          if (a.q_norm_w) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              x1[i] = __fmul_rn(__fmul_rn(x1[i], inv), a.q_norm_w[p0 + i]);
+              x2[i] = __fmul_rn(__fmul_rn(x2[i], inv), a.q_norm_w[HD / 2 + p0 + i]);
+            }
+          }
+          if (crow) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              const float c = crow[p0 + i], s = srow[p0 + i];
+              const float y1 = __fsub_rn(__fmul_rn(x1[i], c), __fmul_rn(x2[i], s));
+              const float y2 = __fadd_rn(__fmul_rn(x2[i], c), __fmul_rn(x1[i], s));
+              x1[i] = y1;
+              x2[i] = y2;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; i++) x1[i] = x2[i] = 0.f;
+        }
+        const int c1 = p0 / 8, c2 = (HD / 2 + p0) / 8;
+        const uint32_t a1 = sQ + (c1 >> 3) * C::TILE128 + sw128_offset(r, c1 & 7);
+        const uint32_t a2 = sQ + (c2 >> 3) * C::TILE128 + sw128_offset(r, c2 & 7);
+        if (SPLIT) {
+          st_chunk_split(a1, a1 + C::HB * C::TILE128, x1);
+          st_chunk_split(a2, a2 + C::HB * C::TILE128, x2);
+        } else {
+          st_chunk<BF16>(a1, x1);
+          st_chunk<BF16>(a2, x2);
+        }
+      }
+      fence_async_smem();
+      mbar_arrive(bar(kBarQ));
+    }
+
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; j++) {
+      const bool got_s = mbar_wait(bar(kBarSFull), j & 1, abort_flag, a.err, kErrTimeoutSoftmax);
+      __syncwarp();  // reconverge before the warp-wide tcgen05.ld
+      if (!__all_sync(0xffffffffu, got_s)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[BN];
+      {
+        uint32_t u[BN];
+#pragma unroll
+        for (int c = 0; c < BN / 32; c++)
+          tmem_ld32(trow + C::S_COL + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < BN; c++) x[c] = __uint_as_float(u[c]) * a.scale_log2;
+      }
+      tc_fence_before();
+      mbar_arrive(bar(kBarSFree));
+      // causal mask on tiles that cross the diagonal
+      const int k0 = j * BN;
+      if (k0 + BN - 1 > q_row) {
+#pragma unroll
+        for (int c = 0; c < BN; c++)
+          if (k0 + c > q_row) x[c] = -INFINITY;
+      }
+      float mt = x[0];
+#pragma unroll
+      for (int c = 1; c < BN; c++) mt = fmaxf(mt, x[c]);
+      const float m_new = fmaxf(m_run, mt);
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; c++) {
+        x[c] = ex2(x[c] - m_new);
+        rs += x[c];
+      }
+      const float corr = ex2(m_run - m_new);
+      l_run = l_run * corr + rs;
+      m_run = m_new;
+      if (j > 0) {
+        const bool got_o =
+            mbar_wait(bar(kBarODone), (j - 1) & 1, abort_flag, a.err, kErrTimeoutSoftmax);
+        __syncwarp();
+        if (!__all_sync(0xffffffffu, got_o)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // tcgen05.ld/st are warp-collective: the branch must be warp-uniform
+        // (a row whose max did not move multiplies by exactly 1).
+        if (__any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; c++) {
+            uint32_t o[32];
+            tmem_ld32(trow + C::O_COL + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+            tmem_st32(trow + C::O_COL + c * 32, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P row -> 16-bit operand (K-major, 128-byte swizzle)
+#pragma unroll
+      for (int ch = 0; ch < BN / 8; ch++) {
+        float f[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) f[i] = x[ch * 8 + i];
+        const uint32_t pa = sP + (ch >> 3) * C::TILE128 + sw128_offset(r, ch & 7);
+        if (SPLIT) st_chunk_split(pa, pa + C::PB * C::TILE128, f);
+        else st_chunk<BF16>(pa, f);
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar(kBarPFull));
+    }
+    // ---- epilogue: O / l -> global
+    bool got_f = ok && mbar_wait(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, a.err,
+                                 kErrTimeoutEpilogue);
+    __syncwarp();
+    if (__all_sync(0xffffffffu, got_f)) {
+      tc_fence_after();
+      const float inv_l = 1.f / l_run;
+      const int64_t obase = (int64_t)q_row * a.o_stride + (int64_t)h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; c++) {
+        uint32_t o[32];
+        tmem_ld32(trow + C::O_COL + c * 32, o);
+        tmem_ld_wait();
+        if (valid) {
+          if (a.dtype_o == kF32) {
+            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.o) + obase + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l,
+                                   __uint_as_float(o[4 * i + 1]) * inv_l,
+                                   __uint_as_float(o[4 * i + 2]) * inv_l,
+                                   __uint_as_float(o[4 * i + 3]) * inv_l);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.o) + obase + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              uint32_t w[4];
+#pragma unroll
+              for (int k = 0; k < 4; k++) {
+                const float lo = __uint_as_float(o[8 * i + 2 * k]) * inv_l;
+                const float hi = __uint_as_float(o[8 * i + 2 * k + 1]) * inv_l;
+                w[k] = a.dtype_o == kBF16 ? pack_bf162(lo, hi) : pack_half2(lo, hi);
+              }
+              dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();  // lane 0 arrives from the MMA loop; dealloc is warp-collective
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D map over a [S][Hkv][hd] 16-bit tensor, box {64, 1, BN}, 128-byte swizzle.
+static bool make_kv_map(CUtensorMap* m, const void* base, int S, int Hkv, int hd, int BN,
+                        bool bf16) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)Hkv, (cuuint64_t)S};
+  cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)Hkv * hd * 2};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)BN};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int HD, int BN, bool SPLIT, bool BF16, int NST>
+static cudaError_t run_prefill(const PrefillArgs& a, const void* k16, const void* v16,
+                               const void* split, cudaStream_t st) {
+  using C = PfCfg<HD, BN, SPLIT, NST>;
+  auto kern = prefill_tc_kernel<HD, BN, SPLIT, BF16, NST>;
+  static unsigned configured = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(__atomic_load_n(&configured, __ATOMIC_ACQUIRE) & (1u << (dev & 31)))) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    __atomic_fetch_or(&configured, 1u << (dev & 31), __ATOMIC_RELEASE);
+  }
+  CUtensorMap mk, mv, mkl, mvl;
+  if (SPLIT) {
+    const size_t plane = (size_t)a.S * a.Hkv * HD;
+    const __half* sp = reinterpret_cast<const __half*>(split);
+    if (!make_kv_map(&mk, sp, a.S, a.Hkv, HD, BN, false) ||
+        !make_kv_map(&mkl, sp + plane, a.S, a.Hkv, HD, BN, false) ||
+        !make_kv_map(&mv, sp + 2 * plane, a.S, a.Hkv, HD, BN, false) ||
+        !make_kv_map(&mvl, sp + 3 * plane, a.S, a.Hkv, HD, BN, false))
+      return cudaErrorInvalidValue;
+  } else {
+    if (!make_kv_map(&mk, k16, a.S, a.Hkv, HD, BN, BF16) ||
+        !make_kv_map(&mv, v16, a.S, a.Hkv, HD, BN, BF16))
+      return cudaErrorInvalidValue;
+    mkl = mk;
+    mvl = mv;
+  }
+  const int n_qt = (a.S + 127) / 128;
+  kern<<<(unsigned)(n_qt * a.H), 256, C::SMEM, st>>>(mk, mv, mkl, mvl, a);
+  return cudaGetLastError();
+}
+
+bool prefill_tc_supported(int hd) { return hd == 64 || hd == 128 || hd == 256; }
+
+cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* k16, const void* v16,
+                              bool bf16, const void* split, cudaStream_t st) {
+  const bool sp = split != nullptr;
+  if (sp) {
+    switch (hd) {
+      case 64: return run_prefill<64, 128, true, false, 2>(a, k16, v16, split, st);
+      case 128: return run_prefill<128, 64, true, false, 2>(a, k16, v16, split, st);
+      case 256: return run_prefill<256, 32, true, false, 1>(a, k16, v16, split, st);
+    }
+  } else if (bf16) {
+    switch (hd) {
+      case 64: return run_prefill<64, 128, false, true, 3>(a, k16, v16, split, st);
+      case 128: return run_prefill<128, 128, false, true, 2>(a, k16, v16, split, st);
+      case 256: return run_prefill<256, 64, false, true, 2>(a, k16, v16, split, st);
+    }
+  } else {
+    switch (hd) {
+      case 64: return run_prefill<64, 128, false, false, 3>(a, k16, v16, split, st);
+      case 128: return run_prefill<128, 128, false, false, 2>(a, k16, v16, split, st);
+      case 256: return run_prefill<256, 64, false, false, 2>(a, k16, v16, split, st);
+    }
+  }
+  return cudaErrorNotSupported;
+}
+
+}  // namespace eb

@@ -1,0 +1,83 @@
+"""CPU-side checks of the C-ABI boundary: the library loads, exports every
+symbol the header declares, validates arguments on the host before touching
+a device, and its host-side RoPE table builder matches the oracle bit for bit."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    names = set()
+    for f in os.listdir(os.path.join(ROOT, "include")):
+        if f.endswith(".h"):
+            txt = open(os.path.join(ROOT, "include", f)).read()
+            names |= set(re.findall(r"^EB_API[^;(]*?\b(eb_\w+)\(", txt, flags=re.M))
+    return names
+
+
+def test_header_declares_the_abi():
+    names = _declared()
+    assert {"eb_attn_prefill", "eb_attn_decode", "eb_rope", "eb_kv_write", "eb_rmsnorm",
+            "eb_attention_prefill", "eb_attention_decode", "eb_attention_decode_batched"} <= names
+
+
+def test_library_exports_every_declared_symbol(eb):
+    L = eb.lib()
+    for n in sorted(_declared()):
+        assert hasattr(L, n), n
+    assert set(eb.EXPORTS) == _declared()
+
+
+def test_rope_tables_match_oracle_bitwise(eb, orc):
+    for (ms, hd, th, ra) in [(64, 128, 1e6, None), (40, 256, 1e6, 32), (8, 4, 1e4, None),
+                             (33, 64, 5e5, 3)]:
+        c1, s1 = eb.rope_tables(ms, hd, th, ra)
+        c2, s2 = orc.rope_tables(ms, hd, th, rope_angles=ra)
+        assert np.array_equal(c1, c2) and np.array_equal(s1, s2)
+
+
+def test_host_validation_precedes_device_work(eb):
+    L = eb.lib()
+    # h % hkv != 0, odd head_dim, pos >= max_seq, kv_write past the cache: rejected on the host
+    assert L.eb_attn_prefill(None, None, None, None, 3, 2, 4, 8, 0.3, None, 0, None) == 1
+    assert L.eb_attn_prefill(None, None, None, None, 2, 2, 4, 7, 0.3, None, 0, None) == 1
+    assert L.eb_attn_decode(None, None, None, None, 4, 2, 16, 8, 16, 0.3, None, 0, None) == 1
+    assert L.eb_kv_write(None, None, 2, 4, 8, 8, 6, None) == 1
+    assert L.eb_rope(None, None, None, None, 1, 1, 7, 0, None) == 1
+    # empty work is a no-op and succeeds without a device
+    assert L.eb_attn_prefill(None, None, None, None, 2, 1, 0, 8, 0.3, None, 0, None) == 0
+    d = eb.make_desc(16, 8, 128, 4096)
+    lay = eb.make_layer()
+    assert L.eb_attention_prefill(ctypes.byref(d), ctypes.byref(lay), 0, None, None, None, None,
+                                  None, None, None, 0, None) == 0
+    bad = eb.make_desc(16, 6, 128, 4096)  # 16 % 6 != 0
+    assert L.eb_attention_prefill(ctypes.byref(bad), ctypes.byref(lay), 4, 1, 1, 1, 1, 1, 1, None,
+                                  0, None) == 1
+    assert L.eb_attention_decode(ctypes.byref(d), ctypes.byref(lay), 4096, 1, 1, 1, 1, 1, 1, None,
+                                 0, None) == 1
+
+
+def test_no_device_is_reported_not_faked(eb):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a device is present")
+    L = eb.lib()
+    # valid arguments, no GPU: the call must refuse, never compute elsewhere
+    assert L.eb_rope(1, 1, 1, 1, 1, 1, 8, 0, None) == 5
+
+
+def test_workspace_sizes(eb):
+    d = eb.make_desc(16, 8, 128, 4096)
+    a = eb.attention_decode_workspace_bytes(d, 1, 2047)
+    b = eb.attention_decode_workspace_bytes(d, 64, 32767)
+    assert a > 0 and b > a and a % 256 == 0
+    assert eb.attention_decode_workspace_bytes(d, 1, 10) == 0  # short context: one CTA per head
+    assert eb.attn_prefill_workspace_bytes(16, 8, 128, 128) == 4 * 128 * 8 * 128 * 2
+    assert eb.attn_prefill_workspace_bytes(2, 1, 5, 8) == 0  # SIMT path
+    f16 = eb.make_desc(32, 8, 128, 8192, dtype_qkv=eb.EB_F16, dtype_cache=eb.EB_F16)
+    assert eb.attention_prefill_workspace_bytes(f16, 8192) == 0  # reads the f16 cache directly
