@@ -27,6 +27,7 @@ EXPORTS = (
     "eb_attention_prefill_kv", "eb_attention_prefill_attend",
     "eb_attention_decode", "eb_attention_decode_batched", "eb_attention_decode_workspace_bytes",
     "eb_workspace_init", "eb_head_concat", "eb_get_device_error",
+    "eb_attention_decode_noalloc",
 )
 
 
@@ -90,6 +91,7 @@ def lib() -> ctypes.CDLL:
                                               _i64, _vp, _vp, _sz, _vp]
     L.eb_attention_decode_workspace_bytes.restype = _sz
     L.eb_attention_decode_workspace_bytes.argtypes = [dp, _i64, _i64]
+    L.eb_attention_decode_noalloc.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
     L.eb_workspace_init.argtypes = [_vp, _sz, _vp]
     L.eb_head_concat.argtypes = [_vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_int32, _vp]
     L.eb_get_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
@@ -242,6 +244,16 @@ def attention_decode_batched(desc, layer, batch, positions, max_pos, q, k, v, kc
                                              _ptr(kcache), _ptr(vcache), cache_batch_stride,
                                              _ptr(o), _ptr(workspace), ws_bytes, _stream(stream)),
            "eb_attention_decode_batched")
+
+
+def attention_decode_noalloc(desc, layer, pos, q, k, v, kcache, vcache, o, stream=None):
+    """eb_attention_decode_noalloc: the decode step using the library's own
+    fixed device scratch instead of a caller workspace (for callers that
+    cannot allocate; calls on one device must not overlap)."""
+    _check(lib().eb_attention_decode_noalloc(ctypes.byref(desc), ctypes.byref(layer), pos,
+                                             _ptr(q), _ptr(k), _ptr(v), _ptr(kcache),
+                                             _ptr(vcache), _ptr(o), _stream(stream)),
+           "eb_attention_decode_noalloc")
 
 
 def workspace_init(workspace, stream=None):

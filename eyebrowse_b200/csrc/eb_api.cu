@@ -111,8 +111,8 @@ static int64_t os_of(const eb_attn_desc* d) {
   return d->o_stride ? d->o_stride : (int64_t)d->n_heads * d->head_dim;
 }
 
-// Shared body of single and batched decode.
-static int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
+// Shared body of single and batched decode (also used by eb_noalloc.cu).
+int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
                        const int32_t* positions, int64_t pos_scalar, int64_t max_pos,
                        const void* q, const void* k, const void* v, void* kc, void* vc,
                        int64_t cache_bstride, void* o, int64_t q_bstride, int64_t kv_bstride,

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/eyebrowse_attn.h"
+
 namespace eb {
 
 // ------------------------------------------------------------- small kernels
@@ -101,6 +103,13 @@ struct DecodeArgs {
 // Returns cudaErrorNotSupported when (hd, cache dtype) has no vector kernel.
 cudaError_t launch_decode(const DecodeArgs& a, int dtype_cache, int batch, cudaStream_t st);
 int decode_rows_per_batch(int hd, int dtype_cache);
+// Shared body of the decode entry points, defined in eb_api.cu: validates
+// the workspace against the split-K plan and launches the decode kernels.
+int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
+                const int32_t* positions, int64_t pos_scalar, int64_t max_pos, const void* q,
+                const void* k, const void* v, void* kc, void* vc, int64_t cache_bstride, void* o,
+                int64_t q_bstride, int64_t kv_bstride, int64_t o_bstride, void* ws, size_t ws_bytes,
+                cudaStream_t st);
 
 // ------------------------------------------------------------- prefill (tcgen05)
 struct PrefillArgs {

@@ -188,6 +188,29 @@ EB_API size_t eb_attention_decode_workspace_bytes(const eb_attn_desc* desc, int6
  * Calls that share one workspace must not overlap on the GPU. */
 EB_API int eb_workspace_init(void* workspace, size_t workspace_bytes, eb_stream_t stream);
 
+/* Size in bytes of the device scratch eb_attention_decode_noalloc owns on
+ * every GPU that loads this library. */
+#define EB_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* eb_attention_decode without a workspace argument, for callers that cannot
+ * allocate device memory: a plugin inside a host framework that owns the
+ * whole device pool and hands the plugin only its inputs and outputs, or a
+ * serving loop that must never call into an allocator between steps. No
+ * counterpart in the reference (its kernels need no scratch).
+ * The split-K scratch is a fixed EB_NOALLOC_SCRATCH_BYTES array inside this
+ * library, held by every GPU that loads it until the process exits. A shape
+ * whose split-K plan needs more (eb_attention_decode_workspace_bytes(desc, 1,
+ * pos) > EB_NOALLOC_SCRATCH_BYTES) is refused with EB_ERR_WORKSPACE before
+ * any device work. The call allocates nothing; its first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture. All calls on a device share the one
+ * array: calls that overlap on the GPU (other streams, other threads) race
+ * and corrupt each other's results; serialise them. Same arguments and
+ * results as eb_attention_decode otherwise. */
+EB_API int eb_attention_decode_noalloc(const eb_attn_desc* desc, const eb_attn_layer* layer,
+                                       int64_t pos, const void* q, const void* k, const void* v,
+                                       void* kcache, void* vcache, void* o, eb_stream_t stream);
+
 /* Head-concat after a head-sharded step: src holds G shards [G][rows][heads_per][hd]
  * (as an all-gather leaves them), dst is [rows][G*heads_per][hd]. dtype is eb_dtype. */
 EB_API int eb_head_concat(const void* src, void* dst, int64_t shards, int64_t rows, int64_t heads_per,
