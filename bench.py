@@ -71,7 +71,7 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, uuid: str | None, period_ms: int = 50):
+    def __init__(self, uuid: str | None, period_ms: int = 25):
         self.uuid = uuid
         self.samples = []  # (t, sm, max, reasons:set)
         self.proc = None
@@ -416,7 +416,7 @@ class DecodeWork:
         return self.bytes_total()
 
 
-def make_workload(name):
+def make_workload(name, batch=None):
     if name == "cfg1":
         return PrefillWork("cfg1 causal GQA prefill S128 H16 Hkv8 hd128 f32 (Qwen3-0.6B layer)",
                            128, 16, 8, 128, 1e6, 0, seed=1)
@@ -434,7 +434,7 @@ def make_workload(name):
         return DecodeWork("cfg4 decode step hd256 f32 pos 4224", 8, 4, 256, 4352, 4224, 1e6, True,
                           v_norm=True, scale=1.0, rope_angles=32, n_rot=8)
     if name == "cfg5":
-        return BatchedDecodeWork()
+        return BatchedDecodeWork(B=batch or 64)
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -459,7 +459,8 @@ def time_steps(fn, steps, warmup, world, stream=None):
 
 def cpu_baseline_prefill(w: PrefillWork, target_s: float = 12.0, threads: int | None = None):
     """Oracle (the reference's CPU attention, restated) on the host cores over a
-    bounded sample: the last rows of the sequence for a few heads."""
+    bounded sample: the last R query rows of the first Hs heads, grown until
+    the sample takes about target_s seconds."""
     from oracle import oracle as orc
     threads = threads or len(os.sched_getaffinity(0))
     S, H, Hkv, hd = w.S, w.H, w.Hkv, w.hd
@@ -467,24 +468,24 @@ def cpu_baseline_prefill(w: PrefillWork, target_s: float = 12.0, threads: int | 
     q = (rng.standard_normal((S, H, hd)).astype(np.float32) * w.in_scale)
     k = (rng.standard_normal((S, Hkv, hd)).astype(np.float32) * w.in_scale)
     v = (rng.standard_normal((S, Hkv, hd)).astype(np.float32) * w.in_scale)
-    heads = (0, min(H, max(1, threads // 2)))
-    nh = heads[1] - heads[0]
-    rows_n, spent, flop = 8, 0.0, 0.0
+    rows_n, nh = min(S, 64), 1
     while True:
         r0 = S - rows_n
         t0 = time.perf_counter()
-        orc.attn_prefill_part(q, k, v, H, Hkv, S, hd, w.scale, (r0, S), heads, threads)
+        orc.attn_prefill_part(q, k, v, H, Hkv, S, hd, w.scale, (r0, S), (0, nh), threads)
         dt = time.perf_counter() - t0
-        if dt >= target_s / 3 or rows_n >= S:
-            f = sum(4.0 * hd * (i + 1) for i in range(r0, S)) * nh
-            spent, flop = dt, f
+        flop = sum(4.0 * hd * (i + 1) for i in range(r0, S)) * nh
+        if dt >= target_s / 2 or (rows_n >= S and nh >= H):
             break
-        grow = max(2, int((target_s / 3) / max(dt, 1e-3)))
-        rows_n = min(S, rows_n * grow)
-    return {"value": flop / spent / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"oracle attn_prefill rows [{S - rows_n},{S}) x heads {list(heads)} of "
-                      f"{w.name.split()[0]} ({flop:.3e} FLOP in {spent:.2f} s, f32, "
-                      f"g++ -O3 -ffp-contract=off, {threads} threads)"}
+        grow = max(2.0, (target_s / 1.5) / max(dt, 1e-3))
+        if rows_n < S:
+            rows_n = min(S, int(rows_n * grow))
+        else:
+            nh = min(H, int(nh * grow) + 1)
+    return {"value": flop / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"oracle attn_prefill rows [{S - rows_n},{S}) x heads [0,{nh}) of "
+                      f"{w.name.split()[0]} ({flop:.3e} FLOP in {dt:.2f} s, f32, "
+                      f"gcc -O3 -ffp-contract=off, {threads} threads)"}
 
 
 def cpu_baseline_decode(w: BatchedDecodeWork, threads: int | None = None, n_seq: int = 4):
@@ -513,7 +514,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    w = make_workload(args.workload)
+    w = make_workload(args.workload, args.batch)
     threads = len(os.sched_getaffinity(0))
     vals = []
     base = None
@@ -562,13 +563,15 @@ def measure(w, rank, world, steps, warmup, peaks, peak_kind, sampler=None):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", default="cfg3")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="cfg5 only: sequences per step (default 64; smaller for profiling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
@@ -584,7 +587,7 @@ def main():
         pass
     sampler = ClockSampler(uuid) if rank == 0 else None
 
-    w = make_workload(args.workload)
+    w = make_workload(args.workload, args.batch)
     res = measure(w, rank, world, args.steps, args.warmup, peaks, peak_kind, sampler)
     is_prefill = isinstance(w, PrefillWork)
     if is_prefill:
