@@ -33,6 +33,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from eyebrowse_b200.sharded import gather_heads, head_shard  # noqa: E402
+
 METRIC = "prefill attn TFLOP/s & decode KV GB/s at 1/2/4/8 B200 vs roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -200,10 +202,9 @@ class PrefillWork:
 
         import eyebrowse_b200 as eb
         self.eb = eb
-        if self.H % world or self.Hkv % world:
-            raise SystemExit(f"{self.name}: {world} ranks do not divide H={self.H}, Hkv={self.Hkv}")
+        sh = head_shard(self.H, self.Hkv, world, rank)
         self.world = world
-        self.Hl, self.Hkvl = self.H // world, self.Hkv // world
+        self.Hl, self.Hkvl = sh.n_heads, sh.n_kv_heads
         tdt = {eb.EB_F32: torch.float32, eb.EB_F16: torch.float16, eb.EB_BF16: torch.bfloat16}[self.dt]
         self.tdt = tdt
         g = torch.Generator(device="cuda").manual_seed(self.seed * 1000 + rank)
@@ -246,10 +247,8 @@ class PrefillWork:
 
     def _gather(self):
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(self.gath, self.o)
-            self.eb.head_concat(self.gath, self.full, self.world, self.S, self.Hl, self.hd,
-                                self.dt)
+            gather_heads(self.o, self.gath, self.full, self.world, self.S, self.Hl, self.hd,
+                         self.dt)
 
     def kernel_only(self):
         """The dominant kernel alone: the tensor-core attention (K/V already in the cache)."""
@@ -307,7 +306,8 @@ class BatchedDecodeWork:
         import eyebrowse_b200 as eb
         self.eb = eb
         self.world = world
-        self.Hl, self.Hkvl = self.H // world, self.Hkv // world
+        sh = head_shard(self.H, self.Hkv, world, rank)
+        self.Hl, self.Hkvl = sh.n_heads, sh.n_kv_heads
         tdt = {0: torch.float32, 1: torch.float16, 2: torch.bfloat16}[self.dt]
         self.tdt = tdt
         g = torch.Generator(device="cuda").manual_seed(self.seed * 1000 + rank)
@@ -340,10 +340,8 @@ class BatchedDecodeWork:
                                          self.q, self.k, self.v, self.kc, self.vc,
                                          self.max_seq * self.Hkvl * self.hd, self.o, self.ws)
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(self.gath, self.o)
-            self.eb.head_concat(self.gath, self.full, self.world, self.B, self.Hl, self.hd,
-                                self.dt)
+            gather_heads(self.o, self.gath, self.full, self.world, self.B, self.Hl, self.hd,
+                         self.dt)
 
     def kernel_only(self):
         self.eb.attention_decode_batched(self.desc, self.layer, self.B, self.posd, self.max_pos,
@@ -457,25 +455,37 @@ def time_steps(fn, steps, warmup, world, stream=None):
     return max_over_ranks(ms, world), (t_wall0, t_wall1)
 
 
-def cpu_baseline_prefill(w: PrefillWork, target_s: float = 12.0, threads: int | None = None):
+_CPU_INPUTS = {}
+
+
+def _cpu_inputs(w: PrefillWork):
+    key = (w.S, w.H, w.Hkv, w.hd, w.in_scale)
+    if key not in _CPU_INPUTS:
+        rng = np.random.default_rng(0)
+        _CPU_INPUTS[key] = tuple(
+            (rng.standard_normal(shape).astype(np.float32) * np.float32(w.in_scale))
+            for shape in ((w.S, w.H, w.hd), (w.S, w.Hkv, w.hd), (w.S, w.Hkv, w.hd)))
+    return _CPU_INPUTS[key]
+
+
+def cpu_baseline_prefill(w: PrefillWork, target_s: float = 12.0, threads: int | None = None,
+                         sample=None):
     """Oracle (the reference's CPU attention, restated) on the host cores over a
     bounded sample: the last R query rows of the first Hs heads, grown until
-    the sample takes about target_s seconds."""
+    the sample takes about target_s seconds. Pass `sample=(R, Hs)` to time a
+    fixed sample."""
     from oracle import oracle as orc
     threads = threads or len(os.sched_getaffinity(0))
     S, H, Hkv, hd = w.S, w.H, w.Hkv, w.hd
-    rng = np.random.default_rng(0)
-    q = (rng.standard_normal((S, H, hd)).astype(np.float32) * w.in_scale)
-    k = (rng.standard_normal((S, Hkv, hd)).astype(np.float32) * w.in_scale)
-    v = (rng.standard_normal((S, Hkv, hd)).astype(np.float32) * w.in_scale)
-    rows_n, nh = min(S, 64), 1
+    q, k, v = _cpu_inputs(w)
+    rows_n, nh = sample if sample else (min(S, 64), 1)
     while True:
         r0 = S - rows_n
         t0 = time.perf_counter()
         orc.attn_prefill_part(q, k, v, H, Hkv, S, hd, w.scale, (r0, S), (0, nh), threads)
         dt = time.perf_counter() - t0
         flop = sum(4.0 * hd * (i + 1) for i in range(r0, S)) * nh
-        if dt >= target_s / 2 or (rows_n >= S and nh >= H):
+        if sample or dt >= target_s / 2 or (rows_n >= S and nh >= H):
             break
         grow = max(2.0, (target_s / 1.5) / max(dt, 1e-3))
         if rows_n < S:
@@ -485,7 +495,8 @@ def cpu_baseline_prefill(w: PrefillWork, target_s: float = 12.0, threads: int | 
     return {"value": flop / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
             "sample": f"oracle attn_prefill rows [{S - rows_n},{S}) x heads [0,{nh}) of "
                       f"{w.name.split()[0]} ({flop:.3e} FLOP in {dt:.2f} s, f32, "
-                      f"gcc -O3 -ffp-contract=off, {threads} threads)"}
+                      f"gcc -O3 -ffp-contract=off, {threads} threads)",
+            "_sample": (rows_n, nh)}
 
 
 def cpu_baseline_decode(w: BatchedDecodeWork, threads: int | None = None, n_seq: int = 4):
@@ -518,10 +529,13 @@ def run_reference(args):
     threads = len(os.sched_getaffinity(0))
     vals = []
     base = None
+    fixed = None
+    per_step = min(6.0, 90.0 / max(1, args.steps + args.warmup))
     for i in range(args.warmup + args.steps):
         if isinstance(w, PrefillWork):
-            b = cpu_baseline_prefill(w, target_s=min(6.0, 60.0 / max(1, args.steps + args.warmup)),
-                                     threads=threads)
+            # the first call sizes the sample to ~per_step seconds; later steps reuse it
+            b = cpu_baseline_prefill(w, target_s=per_step, threads=threads, sample=fixed)
+            fixed = b["_sample"]
         elif isinstance(w, BatchedDecodeWork):
             b = cpu_baseline_decode(w, threads=threads, n_seq=2)
         else:
@@ -535,7 +549,8 @@ def run_reference(args):
             "higher_is_better": True, "data": "synthetic", "dtype": "f32",
             "config": w.describe(1),
             "cpu_baseline": {"value": v, "unit": base["unit"], "cores": base["cores"],
-                             "kind": "port", "sample": base["sample"]},
+                             "kind": "port", "sample": base["sample"]
+                             + f"; median of {args.steps} timed samples"},
             "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "note": "reference = oracle/ C restatement of crates/eyebrowse-kernels/src/testutil.rs "
@@ -650,6 +665,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         if is_prefill:
             cpu = cpu_baseline_prefill(w)
+            cpu.pop("_sample", None)
         elif isinstance(w, BatchedDecodeWork):
             cpu = cpu_baseline_decode(w)
 

@@ -1,0 +1,115 @@
+"""Multi-GPU parity of the head-sharded prefill and batched decode (NCCL).
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N \
+        --master-addr 127.0.0.1 --master-port P tests/mgpu_parity.py
+
+Every rank builds the same seeded full inputs, runs its KV-head group
+through the C ABI, and the outputs are all-gathered and head-concatenated
+on every rank (eyebrowse_b200.sharded.gather_heads). Rank 0 checks the full
+result against the oracle at max-abs <= 2e-3, rel-L2 <= 1e-3 and exits
+non-zero on a mismatch. Not collected by pytest: it needs N processes.
+"""
+import datetime
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def main() -> int:
+    import torch
+    import torch.distributed as dist
+
+    import eyebrowse_b200 as eb
+    from eyebrowse_b200.sharded import gather_heads, head_shard
+    from oracle import oracle as orc
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    ok = True
+    # ---- prefill: config-3 geometry at S=1024 (f16)
+    S, H, Hkv, hd = 1024, 32, 8, 128
+    rng = np.random.default_rng(11)
+    q = orc.round_f16(rng.standard_normal((S, H, hd)).astype(np.float32) * 0.5).reshape(S, H, hd)
+    k = orc.round_f16(rng.standard_normal((S, Hkv, hd)).astype(np.float32) * 0.5).reshape(S, Hkv, hd)
+    v = orc.round_f16(rng.standard_normal((S, Hkv, hd)).astype(np.float32) * 0.5).reshape(S, Hkv, hd)
+    cos, sin = eb.rope_tables(S, hd, 5e5)
+    sh = head_shard(H, Hkv, world, rank)
+    f16 = torch.float16
+    dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(f16).cuda()
+    desc = eb.make_desc(sh.n_heads, sh.n_kv_heads, hd, S, dtype_qkv=eb.EB_F16,
+                        dtype_cache=eb.EB_F16, dtype_out=eb.EB_F16)
+    layer = eb.make_layer(rope_cos=torch.from_numpy(cos).cuda(), rope_sin=torch.from_numpy(sin).cuda())
+    kc = torch.empty(S, sh.n_kv_heads, hd, device="cuda", dtype=f16)
+    vc = torch.empty_like(kc)
+    o = torch.empty(S, sh.n_heads, hd, device="cuda", dtype=f16)
+    eb.attention_prefill(desc, layer, S, dev(q[:, sh.h0:sh.h1]), dev(k[:, sh.kv0:sh.kv1]),
+                         dev(v[:, sh.kv0:sh.kv1]), kc, vc, o, None)
+    gath = torch.empty(world, S, sh.n_heads, hd, device="cuda", dtype=f16)
+    full = torch.empty(S, H, hd, device="cuda", dtype=f16)
+    gather_heads(o, gath, full, world, S, sh.n_heads, hd, eb.EB_F16)
+    torch.cuda.synchronize()
+    if rank == 0:
+        qr = orc.round_f16(orc.rope(q, cos, sin, S, H, hd))
+        kr = orc.round_f16(orc.rope(k, cos, sin, S, Hkv, hd))
+        want = orc.attn_prefill_part(qr, kr, v, H, Hkv, S, hd, hd ** -0.5, (S - 96, S), (0, H),
+                                     nthreads=os.cpu_count() or 8).reshape(S, H, hd)[S - 96:]
+        got = full.float().cpu().numpy()[S - 96:]
+        ma, rl = orc.max_abs(got, want), orc.rel_l2(got, want)
+        print(f"[mgpu] world={world} prefill rows [{S-96},{S}) x {H} heads: max_abs={ma:.2e} "
+              f"rel_l2={rl:.2e}", flush=True)
+        ok &= ma <= 2e-3 and rl <= 1e-3
+    # ---- batched decode: config-5 geometry, 8 sequences, f16 caches
+    B, max_seq = 8, 4096
+    pos = (np.random.default_rng(12).integers(512, max_seq, size=B) - 1).astype(np.int32)
+    kcf = orc.round_f16(rng.standard_normal((B, max_seq, Hkv, hd)).astype(np.float32)).reshape(
+        B, max_seq, Hkv, hd)
+    vcf = orc.round_f16(rng.standard_normal((B, max_seq, Hkv, hd)).astype(np.float32)).reshape(
+        B, max_seq, Hkv, hd)
+    qd = orc.round_f16(rng.standard_normal((B, H, hd)).astype(np.float32)).reshape(B, H, hd)
+    kd = orc.round_f16(rng.standard_normal((B, Hkv, hd)).astype(np.float32)).reshape(B, Hkv, hd)
+    vd = orc.round_f16(rng.standard_normal((B, Hkv, hd)).astype(np.float32)).reshape(B, Hkv, hd)
+    cos, sin = eb.rope_tables(max_seq, hd, 5e5)
+    desc = eb.make_desc(sh.n_heads, sh.n_kv_heads, hd, max_seq, dtype_qkv=eb.EB_F16,
+                        dtype_cache=eb.EB_F16, dtype_out=eb.EB_F16)
+    layer = eb.make_layer(rope_cos=torch.from_numpy(cos).cuda(), rope_sin=torch.from_numpy(sin).cuda())
+    kcd = dev(kcf[:, :, sh.kv0:sh.kv1])
+    vcd = dev(vcf[:, :, sh.kv0:sh.kv1])
+    od = torch.empty(B, sh.n_heads, hd, device="cuda", dtype=f16)
+    ws = eb.alloc_workspace(eb.attention_decode_workspace_bytes(desc, B, int(pos.max())))
+    eb.attention_decode_batched(desc, layer, B, torch.from_numpy(pos).cuda(), int(pos.max()),
+                                dev(qd[:, sh.h0:sh.h1]), dev(kd[:, sh.kv0:sh.kv1]),
+                                dev(vd[:, sh.kv0:sh.kv1]), kcd, vcd,
+                                max_seq * sh.n_kv_heads * hd, od, ws)
+    gath = torch.empty(world, B, sh.n_heads, hd, device="cuda", dtype=f16)
+    fulld = torch.empty(B, H, hd, device="cuda", dtype=f16)
+    gather_heads(od, gath, fulld, world, B, sh.n_heads, hd, eb.EB_F16)
+    torch.cuda.synchronize()
+    if rank == 0:
+        for b in range(B):
+            kcf[b, pos[b]] = orc.round_f16(orc.rope(kd[b], cos, sin, 1, Hkv, hd, int(pos[b]))).reshape(Hkv, hd)
+            vcf[b, pos[b]] = vd[b]
+        qr = np.stack([orc.rope(qd[b], cos, sin, 1, H, hd, int(pos[b])) for b in range(B)])
+        want = orc.attn_decode_batched(qr, kcf, vcf, pos, H, Hkv, hd, max_seq,
+                                       max_seq * Hkv * hd, hd ** -0.5, nthreads=os.cpu_count() or 8)
+        got = fulld.float().cpu().numpy().ravel()
+        ma, rl = orc.max_abs(got, want), orc.rel_l2(got, want)
+        print(f"[mgpu] world={world} batched decode {B} seqs: max_abs={ma:.2e} rel_l2={rl:.2e}",
+              flush=True)
+        ok &= ma <= 2e-3 and rl <= 1e-3
+    flag = torch.tensor([0 if ok else 1], device="cuda")
+    dist.all_reduce(flag)
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        print("[mgpu] PASS" if flag.item() == 0 else "[mgpu] FAIL", flush=True)
+    return int(flag.item() != 0)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
