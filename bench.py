@@ -400,6 +400,7 @@ class DecodeWork:
         nb = eb.attention_decode_workspace_bytes(self.desc, 1, self.pos)
         self.ws = eb.alloc_workspace(nb) if nb else None
         self.i = 0
+        self.full = self.o
         self.launches_per_step = 1
 
     def step(self):

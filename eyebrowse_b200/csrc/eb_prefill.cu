@@ -38,28 +38,49 @@ constexpr int constexpr_pow2ceil(int x) {
   return p;
 }
 
-template <int HD, int BN, bool SPLIT, int NST>
+
+// Tile geometry. NQ query tiles (heads of one GQA group, same rows) share
+// each K/V tile. NSB S buffers per query tile: with one query tile, two S
+// buffers let QK of tile j+1 run while the softmax of tile j works; with two
+// query tiles the other tile's MMAs fill that gap instead.
+template <int HD, int BN, int NQ, bool SPLIT, int NST>
 struct PfCfg {
   static constexpr int NQP = SPLIT ? 2 : 1;  // operand planes (hi, lo)
   static constexpr int HB = HD / 64;         // 64-element boxes along head_dim
-  static constexpr int PB = BN >= 64 ? BN / 64 : 1;
   static constexpr int TILE128 = 128 * 128;  // one [128 rows x 128 B] box
-  static constexpr int Q_BYTES = NQP * HB * TILE128;
-  static constexpr int P_BYTES = NQP * PB * TILE128;
+  static constexpr int QT_BYTES = NQP * HB * TILE128;
+  static constexpr int Q_BYTES = NQ * QT_BYTES;
   static constexpr int KV_BOX = BN * 128;  // one [BN rows x 128 B] box
   static constexpr int K_BYTES = NQP * HB * KV_BOX;
   static constexpr int STAGE_BYTES = 2 * K_BYTES;
-  static constexpr int BAR_OFF = Q_BYTES + P_BYTES + NST * STAGE_BYTES;
+  static constexpr int BAR_OFF = Q_BYTES + NST * STAGE_BYTES;
   static constexpr int SMEM = BAR_OFF + 512 + 1024;  // barriers/flags + alignment slack
-  static constexpr int TMEM_COLS = constexpr_pow2ceil(HD + BN);
-  static constexpr uint32_t O_COL = 0, S_COL = HD;
+  static constexpr int NSB = NQ == 1 ? 2 : 1;
+  // TMEM columns: the O accumulators first ([t*HD, (t+1)*HD)), then the S/P
+  // buffers; every MMA destination starts at a column aligned to its width.
+  static constexpr int S_COL0 = NQ * HD;
+  static constexpr int TMEM_COLS = constexpr_pow2ceil(S_COL0 + NQ * NSB * BN);
+  static constexpr int THREADS = 128 + 128 * NQ;
   static_assert(HD % 64 == 0 && HD <= 256, "head_dim");
   static_assert(BN % 32 == 0 && BN <= 128, "kv tile");
+  static_assert(TMEM_COLS <= 512, "tensor memory budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-// Barrier slots in the barrier area.
-enum { kBarQ = 0, kBarSFull, kBarSFree, kBarPFull, kBarODone, kBarFinal, kBarKV };
+// Barrier slots.
+enum { kBarQ = 0, kBarFinal = 1, kBarS0 = 2 };
+
+// A row's running max only moves (and O is only rescaled) when the new tile's
+// max exceeds it by more than this, in log2 units: p <= 2^8 stays exact in
+// f16/bf16 and in the f32 accumulators, and O/l is unaffected.
+constexpr float kRescaleThreshold = 8.0f;
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 
 __device__ __forceinline__ void load8_any(const void* p, int64_t idx, int dt, float (&f)[8]) {
   if (dt == kF32) {
@@ -118,43 +139,51 @@ __device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, unsign
   }
 }
 
-template <int HD, int BN, bool SPLIT, bool BF16, int NST>
-__global__ void __launch_bounds__(256, 1)
+
+template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NST>
+__global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV,
                       const __grid_constant__ CUtensorMap tmKlo,
                       const __grid_constant__ CUtensorMap tmVlo, PrefillArgs a) {
-  using C = PfCfg<HD, BN, SPLIT, NST>;
+  using C = PfCfg<HD, BN, NQ, SPLIT, NST>;
+  constexpr int NSB = C::NSB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const uint32_t sQ = smem_u32(smem);
-  const uint32_t sP = sQ + C::Q_BYTES;
-  const uint32_t sKV = sP + C::P_BYTES;
+  const uint32_t sKV = sQ + C::Q_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::BAR_OFF + 384);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::BAR_OFF + 392);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const int kKFull0 = kBarKV, kKEmpty0 = kBarKV + NST, kVFull0 = kBarKV + 2 * NST,
-            kVEmpty0 = kBarKV + 3 * NST;
+  // barrier index map
+  constexpr int kSFull0 = kBarS0;                 // [NQ][NSB]
+  constexpr int kPFull0 = kSFull0 + NQ * NSB;     // [NQ]
+  constexpr int kODone0 = kPFull0 + NQ;           // [NQ]
+  constexpr int kKFull0 = kODone0 + NQ;           // [NST] each
+  constexpr int kKEmpty0 = kKFull0 + NST;
+  constexpr int kVFull0 = kKEmpty0 + NST;
+  constexpr int kVEmpty0 = kVFull0 + NST;
+  constexpr int kNumBars = kVEmpty0 + NST;
+  static_assert(kNumBars * 8 <= 384, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (a.S + 127) / 128;
-  const int qt = n_qt - 1 - (int)(blockIdx.x / a.H);  // longest causal rows first
-  const int h = (int)(blockIdx.x % a.H);
-  const int kvh = h / (a.H / a.Hkv);
+  const int n_grp = a.H / NQ;
+  const int qt = n_qt - 1 - (int)(blockIdx.x / n_grp);  // longest causal rows first
+  const int grp = (int)(blockIdx.x % n_grp);
+  const int kvh = (grp * NQ) / (a.H / a.Hkv);
   const int q0 = qt * 128;
   const int kv_rows = min(q0 + 128, a.S);
   const int n_tiles = (kv_rows + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(kBarQ), 128);
-    mbar_init(bar(kBarSFull), 1);
-    mbar_init(bar(kBarSFree), 128);
-    mbar_init(bar(kBarPFull), 128);
-    mbar_init(bar(kBarODone), 1);
+    mbar_init(bar(kBarQ), 128 * NQ);
     mbar_init(bar(kBarFinal), 1);
-    for (int s = 0; s < 4 * NST; s++) mbar_init(bar(kBarKV + s), 1);
+    for (int i = kSFull0; i < kPFull0; i++) mbar_init(bar(i), 1);
+    for (int i = kPFull0; i < kODone0; i++) mbar_init(bar(i), 128);
+    for (int i = kODone0; i < kNumBars; i++) mbar_init(bar(i), 1);
     *abort_flag = 0;
     fence_mbar_init();
     fence_async_smem();
@@ -178,8 +207,8 @@ __global__ void __launch_bounds__(256, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // K tile j and V tile j use ring slot j % NST; K is released when QK_j
-    // completes, V when PV_j completes, so K_{j+1} streams in under PV_j.
+    // K tile j and V tile j use ring slot j % NST; K is released when its QK
+    // MMAs complete, V when its PV MMAs do, so K_{j+1} streams in under PV_j.
     if (lane == 0) {
       int kiss[NST], viss[NST];
       for (int s = 0; s < NST; s++) kiss[s] = viss[s] = 0;
@@ -218,14 +247,14 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Order per tile j: QK_j (overlaps the softmax of tile j-1), then
-    // PV_{j-1} once P_{j-1} is written.
     if (lane == 0) {
-      const uint32_t tS = tmem + C::S_COL, tO = tmem + C::O_COL;
       constexpr uint32_t idesc_qk = idesc_f16(128, BN, BF16, false);
       constexpr uint32_t idesc_pv = idesc_f16(128, HD, BF16, true);
-      auto issue_qk = [&](int st) {
+      // S_t(buffer b) = Q_t K^T
+      auto issue_qk = [&](int t, int b, int st) {
         const uint32_t kst = sKV + st * C::STAGE_BYTES;
+        const uint32_t qb = sQ + t * C::QT_BYTES;
+        const uint32_t tS = tmem + C::S_COL0 + (t * NSB + b) * BN;
         constexpr int NPASS = SPLIT ? 3 : 1;
 #pragma unroll
         for (int pass = 0; pass < NPASS; pass++) {
@@ -234,16 +263,18 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
           for (int kk = 0; kk < HD / 16; kk++) {
             const int hb = kk >> 2, w = kk & 3;
-            const uint64_t ad =
-                sdesc_sw128(sQ + (qa * C::HB + hb) * C::TILE128 + w * 32, 16, 1024);
+            const uint64_t ad = sdesc_sw128(qb + (qa * C::HB + hb) * C::TILE128 + w * 32, 16, 1024);
             const uint64_t bd =
                 sdesc_sw128(kst + (kb * C::HB + hb) * C::KV_BOX + w * 32, 16, 1024);
             umma_ss(tS, ad, bd, idesc_qk, (pass > 0 || kk > 0) ? 1u : 0u);
           }
         }
       };
-      auto issue_pv = [&](int st, bool first) {
+      // O_t += P_t V, P_t read from tensor memory (the S buffer it replaced)
+      auto issue_pv = [&](int t, int b, int st, bool first) {
         const uint32_t vst = sKV + st * C::STAGE_BYTES + C::K_BYTES;
+        const uint32_t tP = tmem + C::S_COL0 + (t * NSB + b) * BN;
+        const uint32_t tO = tmem + t * HD;
         constexpr int NPASS = SPLIT ? 3 : 1;
 #pragma unroll
         for (int pass = 0; pass < NPASS; pass++) {
@@ -251,39 +282,67 @@ __global__ void __launch_bounds__(256, 1)
           const int vb = (pass == 1) ? 1 : 0;
 #pragma unroll
           for (int kk = 0; kk < BN / 16; kk++) {
-            const int pb = kk >> 2, w = kk & 3;
-            const uint64_t ad =
-                sdesc_sw128(sP + (pa * C::PB + pb) * C::TILE128 + w * 32, 16, 1024);
             const uint64_t bd =
                 sdesc_sw128(vst + vb * C::HB * C::KV_BOX + kk * 16 * 128, C::KV_BOX, 1024);
-            umma_ss(tO, ad, bd, idesc_pv, (!first || pass > 0 || kk > 0) ? 1u : 0u);
+            umma_ts(tO, tP + pa * (BN / 2) + kk * 8, bd, idesc_pv,
+                    (!first || pass > 0 || kk > 0) ? 1u : 0u);
           }
         }
       };
-      auto pv_step = [&](int t) -> bool {  // PV for tile t
-        const int pst = t % NST;
-        if (!mbar_wait(bar(kBarPFull), t & 1, abort_flag, a.err, kErrTimeoutMma)) return false;
-        if (!mbar_wait(bar(kVFull0 + pst), (t / NST) & 1, abort_flag, a.err, kErrTimeoutMma))
-          return false;
-        tc_fence_after();
-        issue_pv(pst, t == 0);
-        umma_commit(bar(kBarODone));
-        umma_commit(bar(kVEmpty0 + pst));
-        return true;
-      };
       bool ok = mbar_wait(bar(kBarQ), 0, abort_flag, a.err, kErrTimeoutMma);
       tc_fence_after();
+      if (ok && mbar_wait(bar(kKFull0), 0, abort_flag, a.err, kErrTimeoutMma)) {
+        tc_fence_after();
+#pragma unroll
+        for (int t = 0; t < NQ; t++) {
+          issue_qk(t, 0, 0);
+          umma_commit(bar(kSFull0 + t * NSB));
+        }
+        umma_commit(bar(kKEmpty0));
+      } else {
+        ok = false;
+      }
       for (int j = 0; ok && j < n_tiles; j++) {
         const int st = j % NST;
-        if (!mbar_wait(bar(kKFull0 + st), (j / NST) & 1, abort_flag, a.err, kErrTimeoutMma)) break;
-        if (j > 0 && !mbar_wait(bar(kBarSFree), (j - 1) & 1, abort_flag, a.err, kErrTimeoutMma))
-          break;
-        tc_fence_after();
-        issue_qk(st);
-        umma_commit(bar(kBarSFull));
-        umma_commit(bar(kKEmpty0 + st));
-        if (j > 0 && !pv_step(j - 1)) break;
-        if (j == n_tiles - 1 && !pv_step(j)) break;
+        const int nj = j + 1, nst = nj % NST;
+        if (NSB == 2 && nj < n_tiles) {
+          // single query tile: S(j+1) goes to the other buffer ahead of PV(j)
+          if (!mbar_wait(bar(kKFull0 + nst), (nj / NST) & 1, abort_flag, a.err, kErrTimeoutMma))
+            break;
+          tc_fence_after();
+          issue_qk(0, nj & 1, nst);
+          umma_commit(bar(kSFull0 + (nj & 1)));
+          umma_commit(bar(kKEmpty0 + nst));
+        }
+#pragma unroll
+        for (int t = 0; t < NQ; t++) {
+          if (!mbar_wait(bar(kPFull0 + t), j & 1, abort_flag, a.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          if (t == 0 &&
+              !mbar_wait(bar(kVFull0 + st), (j / NST) & 1, abort_flag, a.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(t, j % NSB, st, j == 0);
+          umma_commit(bar(kODone0 + t));
+          if (NSB == 1 && nj < n_tiles) {
+            // S_t(j+1) overwrites P_t(j): issued after PV_t(j), executed in order
+            if (t == 0 &&
+                !mbar_wait(bar(kKFull0 + nst), (nj / NST) & 1, abort_flag, a.err, kErrTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_qk(t, 0, nst);
+            umma_commit(bar(kSFull0 + t));
+          }
+        }
+        if (!ok) break;
+        umma_commit(bar(kVEmpty0 + st));
+        if (NSB == 1 && nj < n_tiles) umma_commit(bar(kKEmpty0 + nst));
       }
       // Every issued MMA has completed before TMEM is released.
       umma_commit(bar(kBarFinal));
@@ -291,10 +350,13 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax rows
-    const int r = threadIdx.x - 128;  // tile row == TMEM lane
+    const int t = (warp - 4) >> 2;           // query tile of this warpgroup
+    const int r = threadIdx.x - 128 * (1 + t);  // tile row == TMEM lane
+    const int h = grp * NQ + t;
     const int q_row = q0 + r;
     const bool valid = q_row < a.S;
-    const uint32_t trow = tmem + ((uint32_t)((warp - 4) * 32) << 16);
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t qtile = sQ + t * C::QT_BYTES;
     // Q row: RMSNorm (pass 1: sum of squares), then norm + RoPE per 8-wide
     // chunk pair (p, p + HD/2) straight into the swizzled operand.
     {
@@ -339,8 +401,8 @@ __global__ void __launch_bounds__(256, 1)
           for (int i = 0; i < 8; i++) x1[i] = x2[i] = 0.f;
         }
         const int c1 = p0 / 8, c2 = (HD / 2 + p0) / 8;
-        const uint32_t a1 = sQ + (c1 >> 3) * C::TILE128 + sw128_offset(r, c1 & 7);
-        const uint32_t a2 = sQ + (c2 >> 3) * C::TILE128 + sw128_offset(r, c2 & 7);
+        const uint32_t a1 = qtile + (c1 >> 3) * C::TILE128 + sw128_offset(r, c1 & 7);
+        const uint32_t a2 = qtile + (c2 >> 3) * C::TILE128 + sw128_offset(r, c2 & 7);
         if (SPLIT) {
           st_chunk_split(a1, a1 + C::HB * C::TILE128, x1);
           st_chunk_split(a2, a2 + C::HB * C::TILE128, x2);
@@ -353,10 +415,15 @@ __global__ void __launch_bounds__(256, 1)
       mbar_arrive(bar(kBarQ));
     }
 
+    const float sl2 = a.scale_log2;
+    const uint32_t tO = tmem + lane_off + t * HD;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; j++) {
-      const bool got_s = mbar_wait(bar(kBarSFull), j & 1, abort_flag, a.err, kErrTimeoutSoftmax);
+      const int b = j % NSB;
+      const uint32_t tS = tmem + lane_off + C::S_COL0 + (t * NSB + b) * BN;
+      const bool got_s =
+          mbar_wait(bar(kSFull0 + t * NSB + b), (j / NSB) & 1, abort_flag, a.err, kErrTimeoutSoftmax);
       __syncwarp();  // reconverge before the warp-wide tcgen05.ld
       if (!__all_sync(0xffffffffu, got_s)) {
         ok = false;
@@ -368,74 +435,106 @@ __global__ void __launch_bounds__(256, 1)
         uint32_t u[BN];
 #pragma unroll
         for (int c = 0; c < BN / 32; c++)
-          tmem_ld32(trow + C::S_COL + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
+          tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
         tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < BN; c++) x[c] = __uint_as_float(u[c]) * a.scale_log2;
+        for (int c = 0; c < BN; c++) x[c] = __uint_as_float(u[c]);
       }
-      tc_fence_before();
-      mbar_arrive(bar(kBarSFree));
-      // causal mask on tiles that cross the diagonal
+      // causal mask on tiles that cross the diagonal (raw scores)
       const int k0 = j * BN;
       if (k0 + BN - 1 > q_row) {
 #pragma unroll
         for (int c = 0; c < BN; c++)
           if (k0 + c > q_row) x[c] = -INFINITY;
       }
-      float mt = x[0];
+      float mt = fmax3(x[0], x[1], x[2]);
 #pragma unroll
-      for (int c = 1; c < BN; c++) mt = fmaxf(mt, x[c]);
-      const float m_new = fmaxf(m_run, mt);
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < BN; c++) {
-        x[c] = ex2(x[c] - m_new);
-        rs += x[c];
-      }
-      const float corr = ex2(m_run - m_new);
-      l_run = l_run * corr + rs;
-      m_run = m_new;
-      if (j > 0) {
-        const bool got_o =
-            mbar_wait(bar(kBarODone), (j - 1) & 1, abort_flag, a.err, kErrTimeoutSoftmax);
-        __syncwarp();
-        if (!__all_sync(0xffffffffu, got_o)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // tcgen05.ld/st are warp-collective: the branch must be warp-uniform
-        // (a row whose max did not move multiplies by exactly 1).
-        if (__any_sync(0xffffffffu, corr != 1.f)) {
+      for (int c = 3; c + 1 < BN; c += 2) mt = fmax3(mt, x[c], x[c + 1]);
+      if (BN % 2 == 0) mt = fmaxf(mt, x[BN - 1]);
+      const float ms = mt * sl2;
+      // lazy rescale: warp-uniform, since tcgen05.ld/st of O are warp-collective
+      if (__any_sync(0xffffffffu, ms > m_run + kRescaleThreshold)) {
+        const float m_new = fmaxf(m_run, ms);
+        const float corr = ex2(m_run - m_new);
+        if (j > 0) {
+          // PV(j-1) done. Sound as a parity wait: s_full(j) implies PV(0..j-2)
+          // completed (QK(j) is issued after PV(j-2)) and PV(j) needs P(j),
+          // so at most one phase is outstanding here.
+          const bool got_o = mbar_wait(bar(kODone0 + t), (j - 1) & 1, abort_flag, a.err,
+                                       kErrTimeoutSoftmax);
+          __syncwarp();
+          if (!__all_sync(0xffffffffu, got_o)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < HD / 32; c++) {
             uint32_t o[32];
-            tmem_ld32(trow + C::O_COL + c * 32, o);
+            tmem_ld32(tO + c * 32, o);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
-            tmem_st32(trow + C::O_COL + c * 32, o);
+            tmem_st32(tO + c * 32, o);
           }
           tmem_st_wait();
         }
+        l_run *= corr;
+        m_run = m_new;
       }
-      // P row -> 16-bit operand (K-major, 128-byte swizzle)
+      const float neg_m = -m_run;
+      float rs = 0.f;
+      uint32_t ph[BN / 2];
+      uint32_t pl[SPLIT ? BN / 2 : 1];
 #pragma unroll
-      for (int ch = 0; ch < BN / 8; ch++) {
-        float f[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) f[i] = x[ch * 8 + i];
-        const uint32_t pa = sP + (ch >> 3) * C::TILE128 + sw128_offset(r, ch & 7);
-        if (SPLIT) st_chunk_split(pa, pa + C::PB * C::TILE128, f);
-        else st_chunk<BF16>(pa, f);
+      for (int c = 0; c < BN; c += 2) {
+        const float p0 = ex2(fmaf(x[c], sl2, neg_m));
+        const float p1 = ex2(fmaf(x[c + 1], sl2, neg_m));
+        rs += p0 + p1;
+        if (SPLIT) {
+          const __half2 hh = __floats2half2_rn(p0, p1);
+          const float2 hf = __half22float2(hh);
+          ph[c / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+          pl[c / 2] = pack_half2(p0 - hf.x, p1 - hf.y);
+        } else {
+          ph[c / 2] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
+        }
       }
-      fence_async_smem();
+      l_run += rs;
+#pragma unroll
+      for (int c = 0; c < BN / 64; c++)
+        tmem_st32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ph[c * 32]));
+      if (SPLIT) {
+#pragma unroll
+        for (int c = 0; c < BN / 64; c++)
+          tmem_st32(tS + BN / 2 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&pl[c * 32]));
+      }
+      if (BN % 64) {  // BN == 32: one 16-column store per plane
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+            "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tS),
+            "r"(ph[0]), "r"(ph[1]), "r"(ph[2]), "r"(ph[3]), "r"(ph[4]), "r"(ph[5]), "r"(ph[6]),
+            "r"(ph[7]), "r"(ph[8]), "r"(ph[9]), "r"(ph[10]), "r"(ph[11]), "r"(ph[12]),
+            "r"(ph[13]), "r"(ph[14]), "r"(ph[15])
+            : "memory");
+        if (SPLIT)
+          asm volatile(
+              "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+              "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tS + BN / 2),
+              "r"(pl[0]), "r"(pl[1]), "r"(pl[2]), "r"(pl[3]), "r"(pl[4]), "r"(pl[5]),
+              "r"(pl[6]), "r"(pl[7]), "r"(pl[8]), "r"(pl[9]), "r"(pl[10]), "r"(pl[11]),
+              "r"(pl[12]), "r"(pl[13]), "r"(pl[14]), "r"(pl[15])
+              : "memory");
+      }
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(bar(kBarPFull));
+      mbar_arrive(bar(kPFull0 + t));
     }
     // ---- epilogue: O / l -> global
-    bool got_f = ok && mbar_wait(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, a.err,
-                                 kErrTimeoutEpilogue);
+    // Wait on the barrier the MMA thread commits once, after its last MMA: a
+    // parity wait on the per-PV barrier is only sound when at most one phase
+    // is outstanding, and with two S buffers PV(n-2) can still be in flight.
+    bool got_f = ok && mbar_wait(bar(kBarFinal), 0, abort_flag, a.err, kErrTimeoutEpilogue);
     __syncwarp();
     if (__all_sync(0xffffffffu, got_f)) {
       tc_fence_after();
@@ -444,7 +543,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll 1
       for (int c = 0; c < HD / 32; c++) {
         uint32_t o[32];
-        tmem_ld32(trow + C::O_COL + c * 32, o);
+        tmem_ld32(tO + c * 32, o);
         tmem_ld_wait();
         if (valid) {
           if (a.dtype_o == kF32) {
@@ -514,11 +613,11 @@ static bool make_kv_map(CUtensorMap* m, const void* base, int S, int Hkv, int hd
   return r == CUDA_SUCCESS;
 }
 
-template <int HD, int BN, bool SPLIT, bool BF16, int NST>
+template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NST>
 static cudaError_t run_prefill(const PrefillArgs& a, const void* k16, const void* v16,
                                const void* split, cudaStream_t st) {
-  using C = PfCfg<HD, BN, SPLIT, NST>;
-  auto kern = prefill_tc_kernel<HD, BN, SPLIT, BF16, NST>;
+  using C = PfCfg<HD, BN, NQ, SPLIT, NST>;
+  auto kern = prefill_tc_kernel<HD, BN, NQ, SPLIT, BF16, NST>;
   static unsigned configured = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -545,7 +644,7 @@ static cudaError_t run_prefill(const PrefillArgs& a, const void* k16, const void
     mvl = mv;
   }
   const int n_qt = (a.S + 127) / 128;
-  kern<<<(unsigned)(n_qt * a.H), 256, C::SMEM, st>>>(mk, mv, mkl, mvl, a);
+  kern<<<(unsigned)(n_qt * (a.H / NQ)), C::THREADS, C::SMEM, st>>>(mk, mv, mkl, mvl, a);
   return cudaGetLastError();
 }
 
@@ -553,24 +652,35 @@ bool prefill_tc_supported(int hd) { return hd == 64 || hd == 128 || hd == 256; }
 
 cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* k16, const void* v16,
                               bool bf16, const void* split, cudaStream_t st) {
-  const bool sp = split != nullptr;
-  if (sp) {
+  // Two query tiles per CTA when the heads of a GQA group pair up.
+  const bool pair = ((a.H / a.Hkv) % 2) == 0;
+  if (split) {
     switch (hd) {
-      case 64: return run_prefill<64, 128, true, false, 2>(a, k16, v16, split, st);
-      case 128: return run_prefill<128, 64, true, false, 2>(a, k16, v16, split, st);
-      case 256: return run_prefill<256, 32, true, false, 1>(a, k16, v16, split, st);
+      case 64:
+        return pair ? run_prefill<64, 128, 2, true, false, 2>(a, k16, v16, split, st)
+                    : run_prefill<64, 128, 1, true, false, 2>(a, k16, v16, split, st);
+      case 128: return run_prefill<128, 64, 1, true, false, 2>(a, k16, v16, split, st);
+      case 256: return run_prefill<256, 32, 1, true, false, 1>(a, k16, v16, split, st);
     }
   } else if (bf16) {
     switch (hd) {
-      case 64: return run_prefill<64, 128, false, true, 3>(a, k16, v16, split, st);
-      case 128: return run_prefill<128, 128, false, true, 2>(a, k16, v16, split, st);
-      case 256: return run_prefill<256, 64, false, true, 2>(a, k16, v16, split, st);
+      case 64:
+        return pair ? run_prefill<64, 128, 2, false, true, 4>(a, k16, v16, split, st)
+                    : run_prefill<64, 128, 1, false, true, 4>(a, k16, v16, split, st);
+      case 128:
+        return pair ? run_prefill<128, 128, 2, false, true, 2>(a, k16, v16, split, st)
+                    : run_prefill<128, 128, 1, false, true, 2>(a, k16, v16, split, st);
+      case 256: return run_prefill<256, 64, 1, false, true, 2>(a, k16, v16, split, st);
     }
   } else {
     switch (hd) {
-      case 64: return run_prefill<64, 128, false, false, 3>(a, k16, v16, split, st);
-      case 128: return run_prefill<128, 128, false, false, 2>(a, k16, v16, split, st);
-      case 256: return run_prefill<256, 64, false, false, 2>(a, k16, v16, split, st);
+      case 64:
+        return pair ? run_prefill<64, 128, 2, false, false, 4>(a, k16, v16, split, st)
+                    : run_prefill<64, 128, 1, false, false, 4>(a, k16, v16, split, st);
+      case 128:
+        return pair ? run_prefill<128, 128, 2, false, false, 2>(a, k16, v16, split, st)
+                    : run_prefill<128, 128, 1, false, false, 2>(a, k16, v16, split, st);
+      case 256: return run_prefill<256, 64, 1, false, false, 2>(a, k16, v16, split, st);
     }
   }
   return cudaErrorNotSupported;
