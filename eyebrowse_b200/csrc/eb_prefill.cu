@@ -374,41 +374,68 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
       }
       const float* crow = a.cos_t ? a.cos_t + (int64_t)q_row * (HD / 2) : nullptr;
       const float* srow = a.sin_t ? a.sin_t + (int64_t)q_row * (HD / 2) : nullptr;
-      for (int p0 = 0; p0 < HD / 2; p0 += 8) {
-        float x1[8], x2[8];
+      // QB rotation pairs per batch: every global load of a batch is issued
+      // before its shared-memory stores (which the compiler will not cross).
+      constexpr int QB = (NQ == 2 || HD / 2 < 32) ? 16 : 32;
+#pragma unroll 1
+      for (int pb = 0; pb < HD / 2; pb += QB) {
+        float x1[QB], x2[QB];
         if (valid) {
-          load8_any(a.q, qbase + p0, a.dtype_q, x1);
-          load8_any(a.q, qbase + HD / 2 + p0, a.dtype_q, x2);
-          if (a.q_norm_w) {
+#pragma unroll
+          for (int u = 0; u < QB; u += 8) {
+            float f1[8], f2[8];
+            load8_any(a.q, qbase + pb + u, a.dtype_q, f1);
+            load8_any(a.q, qbase + HD / 2 + pb + u, a.dtype_q, f2);
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-              x1[i] = __fmul_rn(__fmul_rn(x1[i], inv), a.q_norm_w[p0 + i]);
-              x2[i] = __fmul_rn(__fmul_rn(x2[i], inv), a.q_norm_w[HD / 2 + p0 + i]);
+              x1[u + i] = f1[i];
+              x2[u + i] = f2[i];
+            }
+          }
+          if (a.q_norm_w) {
+#pragma unroll
+            for (int i = 0; i < QB; i++) {
+              x1[i] = __fmul_rn(__fmul_rn(x1[i], inv), a.q_norm_w[pb + i]);
+              x2[i] = __fmul_rn(__fmul_rn(x2[i], inv), a.q_norm_w[HD / 2 + pb + i]);
             }
           }
           if (crow) {
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-              const float c = crow[p0 + i], s = srow[p0 + i];
-              const float y1 = __fsub_rn(__fmul_rn(x1[i], c), __fmul_rn(x2[i], s));
-              const float y2 = __fadd_rn(__fmul_rn(x2[i], c), __fmul_rn(x1[i], s));
-              x1[i] = y1;
-              x2[i] = y2;
+            for (int i = 0; i < QB; i += 4) {
+              const float4 c4 = *reinterpret_cast<const float4*>(crow + pb + i);
+              const float4 s4 = *reinterpret_cast<const float4*>(srow + pb + i);
+              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+              for (int e = 0; e < 4; e++) {
+                const float y1 = __fsub_rn(__fmul_rn(x1[i + e], cc[e]), __fmul_rn(x2[i + e], ss[e]));
+                const float y2 = __fadd_rn(__fmul_rn(x2[i + e], cc[e]), __fmul_rn(x1[i + e], ss[e]));
+                x1[i + e] = y1;
+                x2[i + e] = y2;
+              }
             }
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 8; i++) x1[i] = x2[i] = 0.f;
+          for (int i = 0; i < QB; i++) x1[i] = x2[i] = 0.f;
         }
-        const int c1 = p0 / 8, c2 = (HD / 2 + p0) / 8;
-        const uint32_t a1 = qtile + (c1 >> 3) * C::TILE128 + sw128_offset(r, c1 & 7);
-        const uint32_t a2 = qtile + (c2 >> 3) * C::TILE128 + sw128_offset(r, c2 & 7);
-        if (SPLIT) {
-          st_chunk_split(a1, a1 + C::HB * C::TILE128, x1);
-          st_chunk_split(a2, a2 + C::HB * C::TILE128, x2);
-        } else {
-          st_chunk<BF16>(a1, x1);
-          st_chunk<BF16>(a2, x2);
+#pragma unroll
+        for (int u = 0; u < QB; u += 8) {
+          float f1[8], f2[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            f1[i] = x1[u + i];
+            f2[i] = x2[u + i];
+          }
+          const int c1 = (pb + u) / 8, c2 = (HD / 2 + pb + u) / 8;
+          const uint32_t a1 = qtile + (c1 >> 3) * C::TILE128 + sw128_offset(r, c1 & 7);
+          const uint32_t a2 = qtile + (c2 >> 3) * C::TILE128 + sw128_offset(r, c2 & 7);
+          if (SPLIT) {
+            st_chunk_split(a1, a1 + C::HB * C::TILE128, f1);
+            st_chunk_split(a2, a2 + C::HB * C::TILE128, f2);
+          } else {
+            st_chunk<BF16>(a1, f1);
+            st_chunk<BF16>(a2, f2);
+          }
         }
       }
       fence_async_smem();
@@ -447,10 +474,19 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
         for (int c = 0; c < BN; c++)
           if (k0 + c > q_row) x[c] = -INFINITY;
       }
-      float mt = fmax3(x[0], x[1], x[2]);
+      // row max: 8 independent chains, then a short tree (keeps the
+      // dependent-latency chain ~BN/16 deep instead of BN/2)
+      float mt;
+      {
+        float mc[8];
 #pragma unroll
-      for (int c = 3; c + 1 < BN; c += 2) mt = fmax3(mt, x[c], x[c + 1]);
-      if (BN % 2 == 0) mt = fmaxf(mt, x[BN - 1]);
+        for (int i = 0; i < 8; i++) mc[i] = fmaxf(x[i], x[i + 8]);
+#pragma unroll
+        for (int c = 16; c < BN; c += 16)
+#pragma unroll
+          for (int i = 0; i < 8; i++) mc[i] = fmax3(mc[i], x[c + i], x[c + 8 + i]);
+        mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[5]), fmaxf(mc[6], mc[7]));
+      }
       const float ms = mt * sl2;
       // lazy rescale: warp-uniform, since tcgen05.ld/st of O are warp-collective
       if (__any_sync(0xffffffffu, ms > m_run + kRescaleThreshold)) {
@@ -483,14 +519,16 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
         m_run = m_new;
       }
       const float neg_m = -m_run;
-      float rs = 0.f;
+      float rsum[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) rsum[i] = 0.f;
       uint32_t ph[BN / 2];
       uint32_t pl[SPLIT ? BN / 2 : 1];
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
         const float p0 = ex2(fmaf(x[c], sl2, neg_m));
         const float p1 = ex2(fmaf(x[c + 1], sl2, neg_m));
-        rs += p0 + p1;
+        rsum[(c >> 1) & 7] += p0 + p1;
         if (SPLIT) {
           const __half2 hh = __floats2half2_rn(p0, p1);
           const float2 hf = __half22float2(hh);
@@ -500,7 +538,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
           ph[c / 2] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
         }
       }
-      l_run += rs;
+      l_run += ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) +
+               ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
 #pragma unroll
       for (int c = 0; c < BN / 64; c++)
         tmem_st32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ph[c * 32]));
@@ -657,8 +696,7 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* k16, con
   if (split) {
     switch (hd) {
       case 64:
-        return pair ? run_prefill<64, 128, 2, true, false, 2>(a, k16, v16, split, st)
-                    : run_prefill<64, 128, 1, true, false, 2>(a, k16, v16, split, st);
+        return run_prefill<64, 128, 1, true, false, 2>(a, k16, v16, split, st);
       case 128: return run_prefill<128, 64, 1, true, false, 2>(a, k16, v16, split, st);
       case 256: return run_prefill<256, 32, 1, true, false, 1>(a, k16, v16, split, st);
     }
