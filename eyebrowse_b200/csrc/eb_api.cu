@@ -70,7 +70,7 @@ static DecodePlan plan_decode(int64_t batch, int64_t h, int64_t hkv, int64_t hd,
     p.cmax = 1;
     return p;
   }
-  const int rpb = decode_rows_per_batch((int)hd, dtype_cache);
+  const int rpb = decode_rows_per_batch((int)hd, dtype_cache, (int)(h / hkv));
   const int64_t target_ctas = 2 * 148;
   int64_t chunk = (rows * batch * hkv + target_ctas - 1) / target_ctas;
   chunk = (chunk + rpb - 1) / rpb * rpb;
@@ -156,6 +156,7 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
     a.H = d->n_heads;
     a.Hkv = d->n_kv_heads;
     a.hd = hd;
+    a.max_seq = d->max_seq;
     a.chunk = p.chunk;
     a.cmax = p.cmax;
     a.eps = d->eps;

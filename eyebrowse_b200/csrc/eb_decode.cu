@@ -268,7 +268,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
   if (tid == 0) *cnt = 0u;
 }
 
-int decode_rows_per_batch(int hd, int dtype_cache) {
+int decode_rows_per_batch(int hd, int dtype_cache, int group) {
+  if (decode_tc_supported(hd, dtype_cache, group)) return 64;  // tensor-core tile rows
   const int vec = dtype_cache == kF32 ? 4 : 8;
   int lpr = hd / vec;
   if (lpr > 32) lpr = 32;
@@ -306,6 +307,8 @@ static cudaError_t launch_hd(const DecodeArgs& a, int dtype_cache, int batch, cu
 }
 
 cudaError_t launch_decode(const DecodeArgs& a, int dtype_cache, int batch, cudaStream_t st) {
+  if (decode_tc_supported(a.hd, dtype_cache, a.H / a.Hkv))
+    return launch_decode_tc(a, dtype_cache, batch, st);
   switch (a.hd) {
     case 64: return launch_hd<64>(a, dtype_cache, batch, st);
     case 128: return launch_hd<128>(a, dtype_cache, batch, st);

@@ -94,6 +94,7 @@ struct DecodeArgs {
   const int32_t* positions;  // device, per sequence; nullptr -> pos_scalar
   int pos_scalar;
   int H, Hkv, hd, chunk, cmax;
+  int max_seq;         // cache rows per sequence (tensor-map extent)
   float eps, scale_log2;
   float* ws_ml;        // [B][H][cmax] x (m, l)
   float* ws_acc;       // [B][H][cmax][hd]
@@ -102,7 +103,10 @@ struct DecodeArgs {
 };
 // Returns cudaErrorNotSupported when (hd, cache dtype) has no vector kernel.
 cudaError_t launch_decode(const DecodeArgs& a, int dtype_cache, int batch, cudaStream_t st);
-int decode_rows_per_batch(int hd, int dtype_cache);
+int decode_rows_per_batch(int hd, int dtype_cache, int group);
+// tcgen05 decode for 16-bit caches (eb_decode_tc.cu)
+bool decode_tc_supported(int hd, int dtype_cache, int group);
+cudaError_t launch_decode_tc(const DecodeArgs& a, int dtype_cache, int batch, cudaStream_t st);
 // Shared body of the decode entry points, defined in eb_api.cu: validates
 // the workspace against the split-K plan and launches the decode kernels.
 int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,

@@ -202,72 +202,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32) prep_kv_kernel(PrepArgs a) {
   }
 }
 
-// Vectorised K/V prep for head_dim = 32*E (64/128/256): the row stays in
-// registers, lane l holds elements [l*E, l*E+E) and the RoPE partner of a
-// first-half element sits in lane l^16 at the same slot. RPW rows per warp,
-// all loads issued before any math.
-template <int E>
-__device__ __forceinline__ void ld_row(const void* p, int64_t i, int dt, float (&f)[E]) {
-  if (dt == kF32) {
-    const float* q = reinterpret_cast<const float*>(p) + i;
-    if constexpr (E % 4 == 0) {
-#pragma unroll
-      for (int k = 0; k < E; k += 4) {
-        const float4 v = *reinterpret_cast<const float4*>(q + k);
-        f[k] = v.x; f[k + 1] = v.y; f[k + 2] = v.z; f[k + 3] = v.w;
-      }
-    } else {
-      const float2 v = *reinterpret_cast<const float2*>(q);
-      f[0] = v.x; f[1] = v.y;
-    }
-  } else {
-    const uint16_t* q = reinterpret_cast<const uint16_t*>(p) + i;
-    uint32_t w[E / 2];
-    if constexpr (E == 8) {
-      const uint4 v = *reinterpret_cast<const uint4*>(q);
-      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-    } else if constexpr (E == 4) {
-      const uint2 v = *reinterpret_cast<const uint2*>(q);
-      w[0] = v.x; w[1] = v.y;
-    } else {
-      w[0] = *reinterpret_cast<const uint32_t*>(q);
-    }
-#pragma unroll
-    for (int k = 0; k < E / 2; k++) {
-      if (dt == kF16) {
-        const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
-        f[2 * k] = t.x; f[2 * k + 1] = t.y;
-      } else {
-        const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-        f[2 * k] = t.x; f[2 * k + 1] = t.y;
-      }
-    }
-  }
-}
-
-template <int E>
-__device__ __forceinline__ void st_row(void* p, int64_t i, int dt, const float (&f)[E]) {
-  if (dt == kF32) {
-    float* q = reinterpret_cast<float*>(p) + i;
-    if constexpr (E % 4 == 0) {
-#pragma unroll
-      for (int k = 0; k < E; k += 4)
-        *reinterpret_cast<float4*>(q + k) = make_float4(f[k], f[k + 1], f[k + 2], f[k + 3]);
-    } else {
-      *reinterpret_cast<float2*>(q) = make_float2(f[0], f[1]);
-    }
-  } else {
-    uint32_t w[E / 2];
-#pragma unroll
-    for (int k = 0; k < E / 2; k++)
-      w[k] = dt == kF16 ? pack_half2(f[2 * k], f[2 * k + 1]) : pack_bf162(f[2 * k], f[2 * k + 1]);
-    uint16_t* q = reinterpret_cast<uint16_t*>(p) + i;
-    if constexpr (E == 8) *reinterpret_cast<uint4*>(q) = make_uint4(w[0], w[1], w[2], w[3]);
-    else if constexpr (E == 4) *reinterpret_cast<uint2*>(q) = make_uint2(w[0], w[1]);
-    else *reinterpret_cast<uint32_t*>(q) = w[0];
-  }
-}
-
+// Vectorised K/V prep for head_dim = 32*E (64/128/256): RPW rows per warp,
+// all loads issued before any math (row helpers in eb_rowops.cuh).
 template <int E>
 __global__ void __launch_bounds__(256) prep_kv_vec_kernel(PrepArgs a) {
   constexpr int HD = 32 * E;
@@ -304,27 +240,9 @@ __global__ void __launch_bounds__(256) prep_kv_vec_kernel(PrepArgs a) {
     const int r = (int)(t / a.hkv);
     const int pos = (a.positions ? a.positions[b] : a.pos0) + r;
     float* v = x[i];
-    const float* w = which ? a.v_norm_w : a.k_norm_w;
-    if (w) {  // RMSNorm (crates/eyebrowse-kernels/src/rmsnorm.rs:34-36 per element)
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; e++) ss = __fadd_rn(ss, __fmul_rn(v[e], v[e]));
-      ss = warp_sum(ss);
-      const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
-#pragma unroll
-      for (int e = 0; e < E; e++) v[e] = __fmul_rn(__fmul_rn(v[e], inv), w[lane * E + e]);
-    }
-    if (!which && a.cos_t) {  // RoPE (crates/eyebrowse-kernels/src/rope.rs:25-30)
-      const float* cr = a.cos_t + (int64_t)pos * (HD / 2) + (lane & 15) * E;
-      const float* sr = a.sin_t + (int64_t)pos * (HD / 2) + (lane & 15) * E;
-#pragma unroll
-      for (int e = 0; e < E; e++) {
-        const float other = __shfl_xor_sync(0xffffffffu, v[e], 16);
-        const float c = cr[e], sn = sr[e];
-        v[e] = lane < 16 ? __fsub_rn(__fmul_rn(v[e], c), __fmul_rn(other, sn))
-                         : __fadd_rn(__fmul_rn(v[e], c), __fmul_rn(other, sn));
-      }
-    }
+    warp_kv_row<E>(x[i], which ? a.v_norm_w : a.k_norm_w, a.eps,
+                   (!which && a.cos_t) ? a.cos_t + (int64_t)pos * (HD / 2) : nullptr,
+                   (!which && a.cos_t) ? a.sin_t + (int64_t)pos * (HD / 2) : nullptr, lane);
 #pragma unroll
     for (int e = 0; e < E; e++) v[e] = round_to(v[e], a.dtype_cache);
     void* cache = which ? a.vcache : a.kcache;
