@@ -51,7 +51,9 @@ __global__ void __launch_bounds__(96)
   using C = DtcCfg<HD, BN, NST>;
   using TC = std::conditional_t<BF16, __nv_bfloat16, __half>;
   constexpr int E = HD / 32;
-  const int c = blockIdx.x, grp = blockIdx.y, b = blockIdx.z;
+  // KV-head group fastest: the heads of one chunk share cache rows (and DRAM
+  // pages) and run side by side
+  const int grp = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
   const int G = a.H / a.Hkv / gsubs;  // query heads handled here (<= 32)
   const int kvh = grp / gsubs, sub = grp % gsubs;
   const int head0 = kvh * (G * gsubs) + sub * G;
@@ -108,8 +110,9 @@ __global__ void __launch_bounds__(96)
     if (lane == 0) {
       int kiss[NST], viss[NST];
       for (int s = 0; s < NST; s++) kiss[s] = viss[s] = 0;
-      // the new row (written by warp 0 before kQ) must be visible to the copies
-      if (mbar_wait(bar(kQ), 0, abort_flag, a.err, kErrTimeoutTma)) {
+      // Only the chunk holding row pos reads the row warp 0 writes before kQ;
+      // every other chunk starts streaming at once.
+      if (!(a.k_new && last_chunk) || mbar_wait(bar(kQ), 0, abort_flag, a.err, kErrTimeoutTma)) {
         for (int j = 0; j < n_tiles; j++) {
           const int st = j % NST;
           const int row = row_begin + j * BN;
@@ -410,7 +413,7 @@ __global__ void __launch_bounds__(96)
         }
         __threadfence();
         __syncwarp();
-        unsigned* cnt = a.ws_cnt + (int64_t)b * gridDim.y + grp;
+        unsigned* cnt = a.ws_cnt + (int64_t)b * gridDim.x + grp;
         unsigned ticket = 0;
         if (lane == 0) ticket = atomicAdd(cnt, 1u);
         ticket = __shfl_sync(0xffffffffu, ticket, 0);
@@ -479,7 +482,7 @@ static cudaError_t run_decode_tc(const DecodeArgs& a, int batch, int gsubs, cuda
   if (!make_cache_map(&mk, a.kcache, batch, a.max_seq, a.Hkv, HD, a.cache_bstride, BN, BF16) ||
       !make_cache_map(&mv, a.vcache, batch, a.max_seq, a.Hkv, HD, a.cache_bstride, BN, BF16))
     return cudaErrorInvalidValue;
-  dim3 grid(a.cmax, a.Hkv * gsubs, batch);
+  dim3 grid(a.Hkv * gsubs, a.cmax, batch);
   kern<<<grid, 96, C::SMEM, st>>>(mk, mv, a, gsubs);
   return cudaGetLastError();
 }
