@@ -75,7 +75,7 @@ static DecodePlan plan_decode(int64_t batch, int64_t h, int64_t hkv, int64_t hd,
   int64_t chunk = (rows * batch * hkv + target_ctas - 1) / target_ctas;
   chunk = (chunk + rpb - 1) / rpb * rpb;
   if (chunk < rpb) chunk = rpb;
-  if (chunk > 1024) chunk = 1024;
+  if (chunk > 8192) chunk = 8192;
   const int64_t min_chunk = (rows + 255) / 256;  // at most 256 partials per head
   if (chunk < min_chunk) chunk = (min_chunk + rpb - 1) / rpb * rpb;
   if (chunk >= rows) {
