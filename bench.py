@@ -186,6 +186,7 @@ class PrefillWork:
         self.theta, self.dt, self.in_scale, self.seed = theta, dt, in_scale, seed
         self.scale = scale if scale is not None else hd ** -0.5
         self.qk_norm, self.v_norm, self.rope_angles = qk_norm, v_norm, rope_angles
+        self.graph_reps = 20 if S <= 1024 else 0  # launch-bound sizes replay a CUDA graph
 
     def flops(self) -> float:
         return 2.0 * self.hd * self.H * self.S * (self.S + 1)
@@ -363,6 +364,7 @@ class DecodeWork:
         self.theta, self.qk_norm, self.v_norm, self.rope_angles = theta, qk_norm, v_norm, rope_angles
         self.scale = scale if scale is not None else hd ** -0.5
         self.n_rot, self.seed = n_rot, seed
+        self.graph_reps = n_rot  # one pass over the rotating caches per graph replay
 
     def describe(self, world):
         return {"workload": self.name, "n_heads": self.H, "n_kv_heads": self.Hkv, "head_dim": self.hd,
@@ -560,20 +562,46 @@ def run_reference(args):
     return 0
 
 
+def graphed(fn, reps: int):
+    """A CUDA graph of `reps` back-to-back calls of fn (captured after a warm
+    call), returned as a function that replays it. Used for workloads whose
+    step is a few microseconds, so host launch overhead does not set the
+    measured time."""
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    return g.replay, g
+
+
 def measure(w, rank, world, steps, warmup, peaks, peak_kind, sampler=None):
-    """Step time, kernel-only time, e2e time for one workload."""
+    """Step time and dominant-kernel time for one workload (CUDA events).
+    Workloads flagged `graph_reps` replay a CUDA graph of that many steps."""
     import torch
     w.setup(rank, world)
-    stream = torch.cuda.current_stream()
+    reps = getattr(w, "graph_reps", 0) if world == 1 else 0
+    step, kern = w.step, w.kernel_only
+    if reps:
+        step, w._g1 = graphed(w.step, reps)
+        kern, w._g2 = graphed(w.kernel_only, reps)
+        steps = max(1, steps // reps)
     if sampler:
         sampler.start()
-    ms, (t0, t1) = time_steps(w.step, steps, warmup, world)
+    ms, (t0, t1) = time_steps(step, steps, warmup, world)
     if sampler:
         sampler.mark(t0, t1)
     # dominant kernel alone (CUDA events on the launching stream)
-    kms, _ = time_steps(w.kernel_only, steps, max(1, warmup), world)
-    out = {"ms_per_step": ms / steps, "kernel_ms": kms / steps}
-    return out
+    kms, _ = time_steps(kern, steps, max(1, warmup), world)
+    n = steps * max(1, reps)
+    return {"ms_per_step": ms / n, "kernel_ms": kms / n, "graph_reps": reps}
 
 
 def main():
@@ -683,6 +711,7 @@ def main():
             "config": dict(w.describe(world), l2="inputs larger than L2 (no flush)"
                            if is_prefill or isinstance(w, BatchedDecodeWork)
                            else "rotating caches larger than L2"),
+            "cuda_graph_steps": res.get("graph_reps", 0),
             "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": peak_unit,
                          "frac": achieved / peak, "traffic": profile_traffic(tkey) if tkey else None,
                          "peak_source": f"{peak_kind} {peak_name}",

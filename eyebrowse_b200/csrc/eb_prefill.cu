@@ -212,8 +212,12 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
           for (int kk = 0; kk < BN / 16; kk++) {
             const uint64_t bd =
                 sdesc_sw128(vst + vb * C::HB * C::KV_BOX + kk * 16 * 128, C::KV_BOX, 1024);
-            umma_ts(tO, tP + pa * (BN / 2) + kk * 8, bd, idesc_pv,
-                    (!first || pass > 0 || kk > 0) ? 1u : 0u);
+            // column of P elements [16kk, 16kk+16) in the softmax's layout
+            constexpr int HALF = BN >= 64 ? 64 : BN;
+            const int blk = (kk * 16) / HALF, within = (kk * 16) % HALF;
+            const uint32_t col = SPLIT ? blk * HALF + within / 2 + pa * (HALF / 2)
+                                       : blk * (HALF / 2) + within / 2;
+            umma_ts(tO, tP + col, bd, idesc_pv, (!first || pass > 0 || kk > 0) ? 1u : 0u);
           }
         }
       };
@@ -385,27 +389,27 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
         break;
       }
       tc_fence_after();
-      float x[BN];
-      {
-        uint32_t u[BN];
-#pragma unroll
-        for (int c = 0; c < BN / 32; c++)
-          tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < BN; c++) x[c] = __uint_as_float(u[c]);
-      }
-      // causal mask on tiles that cross the diagonal (raw scores)
       const int k0 = j * BN;
-      if (k0 + BN - 1 > q_row) {
-#pragma unroll
-        for (int c = 0; c < BN; c++)
-          if (k0 + c > q_row) x[c] = -INFINITY;
-      }
-      // row max: 8 independent chains, then a short tree (keeps the
-      // dependent-latency chain ~BN/16 deep instead of BN/2)
+      const bool diag = k0 + BN - 1 > q_row;  // tile crosses the causal diagonal
+      // pass 1: the row max (the S row is the only live data here)
       float mt;
       {
+        float x[BN];
+        {
+          uint32_t u[BN];
+#pragma unroll
+          for (int c = 0; c < BN / 32; c++)
+            tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < BN; c++) x[c] = __uint_as_float(u[c]);
+        }
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < BN; c++)
+            if (k0 + c > q_row) x[c] = -INFINITY;
+        }
+        // 8 independent chains, then a short tree
         float mc[8];
 #pragma unroll
         for (int i = 0; i < 8; i++) mc[i] = fmaxf(x[i], x[i + 8]);
@@ -446,53 +450,78 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
         l_run *= corr;
         m_run = m_new;
       }
+      // pass 2: re-read S in halves, P = exp2(s*scale - m) -> 16-bit operand in
+      // TMEM over the columns already consumed (P half h lands in S columns
+      // [h*HALF/2, (h+1)*HALF/2), which this pass has read before)
       const float neg_m = -m_run;
       float rsum[8];
 #pragma unroll
       for (int i = 0; i < 8; i++) rsum[i] = 0.f;
-      uint32_t ph[BN / 2];
-      uint32_t pl[SPLIT ? BN / 2 : 1];
+      constexpr int HALF = BN >= 64 ? 64 : BN;
 #pragma unroll
-      for (int c = 0; c < BN; c += 2) {
-        const float p0 = ex2(fmaf(x[c], sl2, neg_m));
-        const float p1 = ex2(fmaf(x[c + 1], sl2, neg_m));
-        rsum[(c >> 1) & 7] += p0 + p1;
-        if (SPLIT) {
-          const __half2 hh = __floats2half2_rn(p0, p1);
-          const float2 hf = __half22float2(hh);
-          ph[c / 2] = *reinterpret_cast<const uint32_t*>(&hh);
-          pl[c / 2] = pack_half2(p0 - hf.x, p1 - hf.y);
-        } else {
-          ph[c / 2] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
+      for (int hbase = 0; hbase < BN; hbase += HALF) {
+        float x[HALF];
+        {
+          uint32_t u[HALF];
+#pragma unroll
+          for (int c = 0; c < HALF / 32; c++)
+            tmem_ld32(tS + hbase + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < HALF; c++) x[c] = __uint_as_float(u[c]);
+        }
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < HALF; c++)
+            if (k0 + hbase + c > q_row) x[c] = -INFINITY;
+        }
+        uint32_t ph[HALF / 2];
+        uint32_t pl[SPLIT ? HALF / 2 : 1];
+#pragma unroll
+        for (int c = 0; c < HALF; c += 2) {
+          const float p0 = ex2(fmaf(x[c], sl2, neg_m));
+          const float p1 = ex2(fmaf(x[c + 1], sl2, neg_m));
+          rsum[(c >> 1) & 7] += p0 + p1;
+          if (SPLIT) {
+            const __half2 hh = __floats2half2_rn(p0, p1);
+            const float2 hf = __half22float2(hh);
+            ph[c / 2] = *reinterpret_cast<const uint32_t*>(&hh);
+            pl[c / 2] = pack_half2(p0 - hf.x, p1 - hf.y);
+          } else {
+            ph[c / 2] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
+          }
+        }
+        // P layout (32-bit TMEM columns, two 16-bit values each): half h of a
+        // plain P takes columns [h*HALF/2, (h+1)*HALF/2); with hi/lo planes
+        // half h takes [h*HALF, (h+1)*HALF), hi first then lo. Either way it
+        // only covers S columns this pass has already read.
+        if constexpr (HALF == 64) {
+          if (SPLIT) {
+            tmem_st32(tS + hbase, ph);
+            tmem_st32(tS + hbase + 32, *reinterpret_cast<uint32_t(*)[32]>(pl));
+          } else {
+            tmem_st32(tS + hbase / 2, ph);
+          }
+        } else {  // BN == 32: one 16-column store per plane
+          asm volatile(
+              "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+              "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tS),
+              "r"(ph[0]), "r"(ph[1]), "r"(ph[2]), "r"(ph[3]), "r"(ph[4]), "r"(ph[5]), "r"(ph[6]),
+              "r"(ph[7]), "r"(ph[8]), "r"(ph[9]), "r"(ph[10]), "r"(ph[11]), "r"(ph[12]),
+              "r"(ph[13]), "r"(ph[14]), "r"(ph[15])
+              : "memory");
+          if (SPLIT)
+            asm volatile(
+                "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+                "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tS + BN / 2),
+                "r"(pl[0]), "r"(pl[1]), "r"(pl[2]), "r"(pl[3]), "r"(pl[4]), "r"(pl[5]),
+                "r"(pl[6]), "r"(pl[7]), "r"(pl[8]), "r"(pl[9]), "r"(pl[10]), "r"(pl[11]),
+                "r"(pl[12]), "r"(pl[13]), "r"(pl[14]), "r"(pl[15])
+                : "memory");
         }
       }
       l_run += ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) +
                ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
-#pragma unroll
-      for (int c = 0; c < BN / 64; c++)
-        tmem_st32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ph[c * 32]));
-      if (SPLIT) {
-#pragma unroll
-        for (int c = 0; c < BN / 64; c++)
-          tmem_st32(tS + BN / 2 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&pl[c * 32]));
-      }
-      if (BN % 64) {  // BN == 32: one 16-column store per plane
-        asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-            "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tS),
-            "r"(ph[0]), "r"(ph[1]), "r"(ph[2]), "r"(ph[3]), "r"(ph[4]), "r"(ph[5]), "r"(ph[6]),
-            "r"(ph[7]), "r"(ph[8]), "r"(ph[9]), "r"(ph[10]), "r"(ph[11]), "r"(ph[12]),
-            "r"(ph[13]), "r"(ph[14]), "r"(ph[15])
-            : "memory");
-        if (SPLIT)
-          asm volatile(
-              "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-              "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tS + BN / 2),
-              "r"(pl[0]), "r"(pl[1]), "r"(pl[2]), "r"(pl[3]), "r"(pl[4]), "r"(pl[5]),
-              "r"(pl[6]), "r"(pl[7]), "r"(pl[8]), "r"(pl[9]), "r"(pl[10]), "r"(pl[11]),
-              "r"(pl[12]), "r"(pl[13]), "r"(pl[14]), "r"(pl[15])
-              : "memory");
-      }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar(kPFull0 + t));

@@ -57,9 +57,10 @@ def test_noalloc_decode_matches_workspace_decode(eb):
 
 def test_noalloc_refuses_shapes_beyond_its_scratch(eb):
     import torch
-    # 128 query heads x hd 256 over 128K positions needs far more than the
-    # fixed scratch: refused on the host, nothing launched.
-    desc = eb.make_desc(128, 8, 256, 131072)
+    # 256 query heads x hd 256 over 128K positions needs more split-K
+    # partials than the fixed scratch holds: refused on the host, nothing
+    # launched.
+    desc = eb.make_desc(256, 8, 256, 131072)
     layer = eb.make_layer()
     assert eb.attention_decode_workspace_bytes(desc, 1, 131071) > 8 << 20
     x = torch.zeros(16, device="cuda")
