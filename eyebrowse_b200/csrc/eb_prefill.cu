@@ -39,7 +39,7 @@ namespace eb {
 // each K/V tile. NSB S buffers per query tile: with one query tile, two S
 // buffers let QK of tile j+1 run while the softmax of tile j works; with two
 // query tiles the other tile's MMAs fill that gap instead.
-template <int HD, int BN, int NQ, bool SPLIT, int NST>
+template <int HD, int BN, int NQ, bool SPLIT, int NSTK, int NSTV>
 struct PfCfg {
   static constexpr int NQP = SPLIT ? 2 : 1;  // operand planes (hi, lo)
   static constexpr int HB = HD / 64;         // 64-element boxes along head_dim
@@ -47,9 +47,9 @@ struct PfCfg {
   static constexpr int QT_BYTES = NQP * HB * TILE128;
   static constexpr int Q_BYTES = NQ * QT_BYTES;
   static constexpr int KV_BOX = BN * 128;  // one [BN rows x 128 B] box
-  static constexpr int K_BYTES = NQP * HB * KV_BOX;
-  static constexpr int STAGE_BYTES = 2 * K_BYTES;
-  static constexpr int BAR_OFF = Q_BYTES + NST * STAGE_BYTES;
+  static constexpr int K_BYTES = NQP * HB * KV_BOX;  // one K (or V) tile, all planes
+  static constexpr int V_OFF = Q_BYTES + NSTK * K_BYTES;  // V ring follows the K ring
+  static constexpr int BAR_OFF = V_OFF + NSTV * K_BYTES;
   static constexpr int SMEM = BAR_OFF + 512 + 1024;  // barriers/flags + alignment slack
   static constexpr int NSB = NQ == 1 ? 2 : 1;
   // TMEM columns: the O accumulators first ([t*HD, (t+1)*HD)), then the S/P
@@ -68,19 +68,19 @@ enum { kBarQ = 0, kBarFinal = 1, kBarS0 = 2 };
 
 
 
-template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NST>
-__global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
+template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV>
+__global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV,
                       const __grid_constant__ CUtensorMap tmKlo,
                       const __grid_constant__ CUtensorMap tmVlo, PrefillArgs a) {
-  using C = PfCfg<HD, BN, NQ, SPLIT, NST>;
+  using C = PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>;
   constexpr int NSB = C::NSB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const uint32_t sQ = smem_u32(smem);
-  const uint32_t sKV = sQ + C::Q_BYTES;
+  const uint32_t sK = sQ + C::Q_BYTES, sV = sQ + C::V_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::BAR_OFF + 384);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::BAR_OFF + 392);
@@ -89,11 +89,11 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
   constexpr int kSFull0 = kBarS0;                 // [NQ][NSB]
   constexpr int kPFull0 = kSFull0 + NQ * NSB;     // [NQ]
   constexpr int kODone0 = kPFull0 + NQ;           // [NQ]
-  constexpr int kKFull0 = kODone0 + NQ;           // [NST] each
-  constexpr int kKEmpty0 = kKFull0 + NST;
-  constexpr int kVFull0 = kKEmpty0 + NST;
-  constexpr int kVEmpty0 = kVFull0 + NST;
-  constexpr int kNumBars = kVEmpty0 + NST;
+  constexpr int kKFull0 = kODone0 + NQ;           // [NSTK]
+  constexpr int kKEmpty0 = kKFull0 + NSTK;        // [NSTK]
+  constexpr int kVFull0 = kKEmpty0 + NSTK;        // [NSTV]
+  constexpr int kVEmpty0 = kVFull0 + NSTV;        // [NSTV]
+  constexpr int kNumBars = kVEmpty0 + NSTV;
   static_assert(kNumBars * 8 <= 384, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -135,43 +135,46 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // K tile j and V tile j use ring slot j % NST; K is released when its QK
-    // MMAs complete, V when its PV MMAs do, so K_{j+1} streams in under PV_j.
+    // K tile j uses K slot j % NSTK and is released when its QK MMAs
+    // complete; V tile j uses V slot j % NSTV, released after its PV MMAs.
+    // K gets the deeper ring: K_{j+1} is needed one step after K_{j+1-NSTK}
+    // frees, V_{j+1} two steps after V_{j+1-NSTV}.
     if (lane == 0) {
-      int kiss[NST], viss[NST];
-      for (int s = 0; s < NST; s++) kiss[s] = viss[s] = 0;
+      int kiss[NSTK], viss[NSTV];
+      for (int s = 0; s < NSTK; s++) kiss[s] = 0;
+      for (int s = 0; s < NSTV; s++) viss[s] = 0;
       for (int j = 0; j < n_tiles; j++) {
-        const int st = j % NST;
-        const uint32_t kst = sKV + st * C::STAGE_BYTES;
-        const uint32_t vst = kst + C::K_BYTES;
-        if (j >= NST &&
-            !mbar_wait(bar(kKEmpty0 + st), (j / NST - 1) & 1, abort_flag, a.err, kErrTimeoutTma))
+        const int sk = j % NSTK, sv = j % NSTV;
+        const uint32_t kst = sK + sk * C::K_BYTES;
+        const uint32_t vst = sV + sv * C::K_BYTES;
+        if (j >= NSTK && !mbar_wait(bar(kKEmpty0 + sk), (j / NSTK - 1) & 1, abort_flag, a.err,
+                                    kErrTimeoutTma))
           break;
-        const uint32_t kf = bar(kKFull0 + st);
+        const uint32_t kf = bar(kKFull0 + sk);
         mbar_arrive_expect_tx(kf, C::K_BYTES);
 #pragma unroll
         for (int hb = 0; hb < C::HB; hb++) {
           tma_load_3d(kst + hb * C::KV_BOX, &tmK, kf, hb * 64, kvh, j * BN);
           if (SPLIT) tma_load_3d(kst + (C::HB + hb) * C::KV_BOX, &tmKlo, kf, hb * 64, kvh, j * BN);
         }
-        kiss[st]++;
-        if (j >= NST &&
-            !mbar_wait(bar(kVEmpty0 + st), (j / NST - 1) & 1, abort_flag, a.err, kErrTimeoutTma))
+        kiss[sk]++;
+        if (j >= NSTV && !mbar_wait(bar(kVEmpty0 + sv), (j / NSTV - 1) & 1, abort_flag, a.err,
+                                    kErrTimeoutTma))
           break;
-        const uint32_t vf = bar(kVFull0 + st);
+        const uint32_t vf = bar(kVFull0 + sv);
         mbar_arrive_expect_tx(vf, C::K_BYTES);
 #pragma unroll
         for (int hb = 0; hb < C::HB; hb++) {
           tma_load_3d(vst + hb * C::KV_BOX, &tmV, vf, hb * 64, kvh, j * BN);
           if (SPLIT) tma_load_3d(vst + (C::HB + hb) * C::KV_BOX, &tmVlo, vf, hb * 64, kvh, j * BN);
         }
-        viss[st]++;
+        viss[sv]++;
       }
       // Every issued copy has landed before the CTA can exit.
-      for (int s = 0; s < NST; s++) {
+      for (int s = 0; s < NSTK; s++)
         if (kiss[s]) mbar_drain(bar(kKFull0 + s), (kiss[s] - 1) & 1, a.err, kErrTimeoutTma);
+      for (int s = 0; s < NSTV; s++)
         if (viss[s]) mbar_drain(bar(kVFull0 + s), (viss[s] - 1) & 1, a.err, kErrTimeoutTma);
-      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -179,8 +182,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
       constexpr uint32_t idesc_qk = idesc_f16(128, BN, BF16, false);
       constexpr uint32_t idesc_pv = idesc_f16(128, HD, BF16, true);
       // S_t(buffer b) = Q_t K^T
-      auto issue_qk = [&](int t, int b, int st) {
-        const uint32_t kst = sKV + st * C::STAGE_BYTES;
+      auto issue_qk = [&](int t, int b, int sk) {
+        const uint32_t kst = sK + sk * C::K_BYTES;
         const uint32_t qb = sQ + t * C::QT_BYTES;
         const uint32_t tS = tmem + C::S_COL0 + (t * NSB + b) * BN;
         constexpr int NPASS = SPLIT ? 3 : 1;
@@ -199,8 +202,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
         }
       };
       // O_t += P_t V, P_t read from tensor memory (the S buffer it replaced)
-      auto issue_pv = [&](int t, int b, int st, bool first) {
-        const uint32_t vst = sKV + st * C::STAGE_BYTES + C::K_BYTES;
+      auto issue_pv = [&](int t, int b, int sv, bool first) {
+        const uint32_t vst = sV + sv * C::K_BYTES;
         const uint32_t tP = tmem + C::S_COL0 + (t * NSB + b) * BN;
         const uint32_t tO = tmem + t * HD;
         constexpr int NPASS = SPLIT ? 3 : 1;
@@ -235,16 +238,16 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
         ok = false;
       }
       for (int j = 0; ok && j < n_tiles; j++) {
-        const int st = j % NST;
-        const int nj = j + 1, nst = nj % NST;
+        const int sv = j % NSTV;
+        const int nj = j + 1, nsk = nj % NSTK;
         if (NSB == 2 && nj < n_tiles) {
           // single query tile: S(j+1) goes to the other buffer ahead of PV(j)
-          if (!mbar_wait(bar(kKFull0 + nst), (nj / NST) & 1, abort_flag, a.err, kErrTimeoutMma))
+          if (!mbar_wait(bar(kKFull0 + nsk), (nj / NSTK) & 1, abort_flag, a.err, kErrTimeoutMma))
             break;
           tc_fence_after();
-          issue_qk(0, nj & 1, nst);
+          issue_qk(0, nj & 1, nsk);
           umma_commit(bar(kSFull0 + (nj & 1)));
-          umma_commit(bar(kKEmpty0 + nst));
+          umma_commit(bar(kKEmpty0 + nsk));
         }
 #pragma unroll
         for (int t = 0; t < NQ; t++) {
@@ -253,28 +256,28 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NST>::THREADS, 1)
             break;
           }
           if (t == 0 &&
-              !mbar_wait(bar(kVFull0 + st), (j / NST) & 1, abort_flag, a.err, kErrTimeoutMma)) {
+              !mbar_wait(bar(kVFull0 + sv), (j / NSTV) & 1, abort_flag, a.err, kErrTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(t, j % NSB, st, j == 0);
+          issue_pv(t, j % NSB, sv, j == 0);
           umma_commit(bar(kODone0 + t));
           if (NSB == 1 && nj < n_tiles) {
             // S_t(j+1) overwrites P_t(j): issued after PV_t(j), executed in order
             if (t == 0 &&
-                !mbar_wait(bar(kKFull0 + nst), (nj / NST) & 1, abort_flag, a.err, kErrTimeoutMma)) {
+                !mbar_wait(bar(kKFull0 + nsk), (nj / NSTK) & 1, abort_flag, a.err, kErrTimeoutMma)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_qk(t, 0, nst);
+            issue_qk(t, 0, nsk);
             umma_commit(bar(kSFull0 + t));
           }
         }
         if (!ok) break;
-        umma_commit(bar(kVEmpty0 + st));
-        if (NSB == 1 && nj < n_tiles) umma_commit(bar(kKEmpty0 + nst));
+        umma_commit(bar(kVEmpty0 + sv));
+        if (NSB == 1 && nj < n_tiles) umma_commit(bar(kKEmpty0 + nsk));
       }
       // Every issued MMA has completed before TMEM is released.
       umma_commit(bar(kBarFinal));
@@ -609,11 +612,11 @@ bool make_kv_map(CUtensorMap* m, const void* base, int S, int Hkv, int hd, int B
   return r == CUDA_SUCCESS;
 }
 
-template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NST>
+template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV>
 static cudaError_t run_prefill(const PrefillArgs& a, const void* k16, const void* v16,
                                const void* split, cudaStream_t st) {
-  using C = PfCfg<HD, BN, NQ, SPLIT, NST>;
-  auto kern = prefill_tc_kernel<HD, BN, NQ, SPLIT, BF16, NST>;
+  using C = PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>;
+  auto kern = prefill_tc_kernel<HD, BN, NQ, SPLIT, BF16, NSTK, NSTV>;
   static unsigned configured = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -653,29 +656,29 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* k16, con
   if (split) {
     switch (hd) {
       case 64:
-        return run_prefill<64, 128, 1, true, false, 2>(a, k16, v16, split, st);
-      case 128: return run_prefill<128, 64, 1, true, false, 2>(a, k16, v16, split, st);
-      case 256: return run_prefill<256, 32, 1, true, false, 1>(a, k16, v16, split, st);
+        return run_prefill<64, 128, 1, true, false, 2, 2>(a, k16, v16, split, st);
+      case 128: return run_prefill<128, 64, 1, true, false, 2, 2>(a, k16, v16, split, st);
+      case 256: return run_prefill<256, 32, 1, true, false, 1, 1>(a, k16, v16, split, st);
     }
   } else if (bf16) {
     switch (hd) {
       case 64:
-        return pair ? run_prefill<64, 128, 2, false, true, 4>(a, k16, v16, split, st)
-                    : run_prefill<64, 128, 1, false, true, 4>(a, k16, v16, split, st);
+        return pair ? run_prefill<64, 128, 2, false, true, 4, 3>(a, k16, v16, split, st)
+                    : run_prefill<64, 128, 1, false, true, 4, 3>(a, k16, v16, split, st);
       case 128:
-        return pair ? run_prefill<128, 128, 2, false, true, 2>(a, k16, v16, split, st)
-                    : run_prefill<128, 128, 1, false, true, 2>(a, k16, v16, split, st);
-      case 256: return run_prefill<256, 64, 1, false, true, 2>(a, k16, v16, split, st);
+        return pair ? run_prefill<128, 128, 2, false, true, 3, 2>(a, k16, v16, split, st)
+                    : run_prefill<128, 128, 1, false, true, 3, 2>(a, k16, v16, split, st);
+      case 256: return run_prefill<256, 64, 1, false, true, 2, 2>(a, k16, v16, split, st);
     }
   } else {
     switch (hd) {
       case 64:
-        return pair ? run_prefill<64, 128, 2, false, false, 4>(a, k16, v16, split, st)
-                    : run_prefill<64, 128, 1, false, false, 4>(a, k16, v16, split, st);
+        return pair ? run_prefill<64, 128, 2, false, false, 4, 3>(a, k16, v16, split, st)
+                    : run_prefill<64, 128, 1, false, false, 4, 3>(a, k16, v16, split, st);
       case 128:
-        return pair ? run_prefill<128, 128, 2, false, false, 2>(a, k16, v16, split, st)
-                    : run_prefill<128, 128, 1, false, false, 2>(a, k16, v16, split, st);
-      case 256: return run_prefill<256, 64, 1, false, false, 2>(a, k16, v16, split, st);
+        return pair ? run_prefill<128, 128, 2, false, false, 3, 2>(a, k16, v16, split, st)
+                    : run_prefill<128, 128, 1, false, false, 3, 2>(a, k16, v16, split, st);
+      case 256: return run_prefill<256, 64, 1, false, false, 2, 2>(a, k16, v16, split, st);
     }
   }
   return cudaErrorNotSupported;
