@@ -237,7 +237,7 @@ class PrefillWork:
             self.full = torch.empty(S, self.H, hd, device="cuda", dtype=tdt)
         else:
             self.full = self.o
-        self.launches_per_step = 2 + (1 if world > 1 else 0)
+        self.launches_per_step = 3 + (1 if world > 1 else 0)  # K/V prep, q prep, attention
         self.bytes_in = sum(t.numel() * t.element_size() for t in (self.q, self.k, self.v))
 
     def step(self):

@@ -247,10 +247,19 @@ const char* eb_status_string(int status) {
 const char* eb_version(void) { return "eyebrowse-b200 0.1 (sm_100a)"; }
 
 // ---------------------------------------------------------------- kernel-level
-size_t eb_attn_prefill_workspace_bytes(int64_t h, int64_t hkv, int64_t s, int64_t hd) {
-  (void)h;
-  if (!prefill_tc_supported((int)hd) || s <= 0 || hkv <= 0) return 0;
+// Tensor-core prefill workspace: [f16 hi/lo K and V planes, when the K/V
+// values are f32][the prepared query rows: one 16-bit plane, or f16 hi/lo
+// planes when split].
+static size_t kv_split_bytes(int64_t s, int64_t hkv, int64_t hd) {
   return round_up((size_t)4 * s * hkv * hd * sizeof(__half));
+}
+static size_t q_prep_bytes(int64_t s, int64_t h, int64_t hd, bool split) {
+  return round_up((size_t)(split ? 2 : 1) * s * h * hd * sizeof(__half));
+}
+
+size_t eb_attn_prefill_workspace_bytes(int64_t h, int64_t hkv, int64_t s, int64_t hd) {
+  if (!prefill_tc_supported((int)hd) || s <= 0 || hkv <= 0 || h <= 0) return 0;
+  return kv_split_bytes(s, hkv, hd) + q_prep_bytes(s, h, hd, true);
 }
 
 int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, int64_t h,
@@ -279,10 +288,21 @@ int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, in
     pa.batch = 1;
     cudaError_t e = launch_prep_kv(pa, st);
     if (e != cudaSuccess) return cuda_status(e);
+    // q rows -> f16 hi/lo planes (k-only prep: no norm, no RoPE here)
+    void* qplanes = static_cast<char*>(workspace) + kv_split_bytes(s, hkv, hd);
+    PrepArgs qa{};
+    qa.k = q;
+    qa.dtype_kv = kF32;
+    qa.kv_stride = h * hd;
+    qa.dtype_cache = kF32;
+    qa.split = qplanes;
+    qa.rows = (int)s;
+    qa.hkv = (int)h;
+    qa.hd = (int)hd;
+    qa.batch = 1;
+    e = launch_prep_kv(qa, st);
+    if (e != cudaSuccess) return cuda_status(e);
     PrefillArgs a{};
-    a.q = q;
-    a.dtype_q = kF32;
-    a.q_stride = h * hd;
     a.o = o;
     a.dtype_o = kF32;
     a.o_stride = h * hd;
@@ -292,7 +312,8 @@ int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, in
     a.scale_log2 = scale * kLog2e;
     a.err = error_word_ptr();
     if (!a.err) return EB_ERR_CUDA;
-    return cuda_status(launch_prefill_tc(a, (int)hd, nullptr, nullptr, false, workspace, st));
+    return cuda_status(
+        launch_prefill_tc(a, (int)hd, qplanes, nullptr, nullptr, false, workspace, st));
   }
   SimtArgs sa{};
   sa.q = q;
@@ -399,8 +420,10 @@ int eb_rope_tables(float* cos_t, float* sin_t, int64_t max_seq, int64_t head_dim
 // ---------------------------------------------------------------- fused primitive
 size_t eb_attention_prefill_workspace_bytes(const eb_attn_desc* d, int64_t seq) {
   if (!desc_ok(d) || seq <= 0) return 0;
-  if (!prefill_tc_supported(d->head_dim) || d->dtype_cache != EB_F32) return 0;
-  return round_up((size_t)4 * seq * d->n_kv_heads * d->head_dim * sizeof(__half));
+  if (!prefill_tc_supported(d->head_dim)) return 0;
+  const bool split = d->dtype_cache == EB_F32;
+  return (split ? kv_split_bytes(seq, d->n_kv_heads, d->head_dim) : 0) +
+         q_prep_bytes(seq, d->n_heads, d->head_dim, split);
 }
 
 // Shared argument checks of the prefill entry points.
@@ -411,7 +434,7 @@ static int prefill_check(const eb_attn_desc* d, const eb_attn_layer* L, int64_t 
   const float* sin_t = L ? L->rope_sin : nullptr;
   if ((cos_t == nullptr) != (sin_t == nullptr)) return EB_ERR_INVALID_ARGUMENT;
   if (seq == 0) return EB_OK;
-  if (prefill_tc_supported(d->head_dim) && d->dtype_cache == EB_F32) {
+  if (prefill_tc_supported(d->head_dim)) {
     const size_t need = eb_attention_prefill_workspace_bytes(d, seq);
     if (!ws || ws_bytes < need || !aligned16(ws)) return EB_ERR_WORKSPACE;
   }
@@ -464,14 +487,28 @@ int eb_attention_prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, i
     if (!aligned16(q) || !aligned16(o) || !aligned16(kcache) || !aligned16(vcache) ||
         ((qs_of(d) * eq) & 15) || ((os_of(d) * eo) & 15))
       return EB_ERR_INVALID_ARGUMENT;
+    // q -> RMSNorm(q_norm_w) -> RoPE -> the MMA operand type (or f16 hi/lo
+    // planes), the same row transform the k rows get
+    void* qprep = static_cast<char*>(workspace) +
+                  (split ? kv_split_bytes(seq, d->n_kv_heads, hd) : 0);
+    PrepArgs qa{};
+    qa.k = q;
+    qa.dtype_kv = d->dtype_qkv;
+    qa.kv_stride = qs_of(d);
+    qa.kcache = split ? nullptr : qprep;
+    qa.dtype_cache = d->dtype_cache;
+    qa.split = split ? qprep : nullptr;
+    qa.rows = (int)seq;
+    qa.hkv = d->n_heads;
+    qa.hd = hd;
+    qa.k_norm_w = L ? L->q_norm_w : nullptr;
+    qa.cos_t = cos_t;
+    qa.sin_t = sin_t;
+    qa.eps = d->eps;
+    qa.batch = 1;
+    cudaError_t e = launch_prep_kv(qa, st);
+    if (e != cudaSuccess) return cuda_status(e);
     PrefillArgs a{};
-    a.q = q;
-    a.dtype_q = d->dtype_qkv;
-    a.q_stride = qs_of(d);
-    a.q_norm_w = L ? L->q_norm_w : nullptr;
-    a.cos_t = cos_t;
-    a.sin_t = sin_t;
-    a.eps = d->eps;
     a.o = o;
     a.dtype_o = d->dtype_out;
     a.o_stride = os_of(d);
@@ -481,8 +518,9 @@ int eb_attention_prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, i
     a.scale_log2 = d->scale * kLog2e;
     a.err = error_word_ptr();
     if (!a.err) return EB_ERR_CUDA;
-    return cuda_status(launch_prefill_tc(a, hd, kcache, vcache, d->dtype_cache == EB_BF16,
-                                         split ? workspace : nullptr, st));
+    return cuda_status(launch_prefill_tc(a, hd, qprep, kcache, vcache,
+                                         d->dtype_cache == EB_BF16, split ? workspace : nullptr,
+                                         st));
   }
   SimtArgs s{};
   s.q = q;

@@ -26,6 +26,8 @@ cudaError_t launch_head_concat(const void* src, void* dst, int64_t shards, int64
 // path: split = [khi | klo | vhi | vlo], each rows*hkv*hd halves, of the values
 // as stored (cache-rounded). batch > 1 handles `batch` sequences, each with
 // its own position (positions[b]) and cache (cache + b*cache_bstride).
+// v == nullptr prepares k rows only (split = [khi | klo]): the query rows of a
+// prefill go through this path (q_norm_w as k_norm_w, hkv = query heads).
 struct PrepArgs {
   const void* k;
   const void* v;
@@ -117,13 +119,6 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
 
 // ------------------------------------------------------------- prefill (tcgen05)
 struct PrefillArgs {
-  const void* q;
-  int dtype_q;
-  int64_t q_stride;
-  const float* q_norm_w;
-  const float* cos_t;
-  const float* sin_t;
-  float eps;
   void* o;
   int dtype_o;
   int64_t o_stride;
@@ -131,10 +126,13 @@ struct PrefillArgs {
   float scale_log2;
   unsigned* err;
 };
-// kv16: 16-bit K/V rows [S][Hkv][hd] the tensor cores read (the cache when it
-// is f16/bf16). split: f16 hi/lo planes when the inputs are f32 (kv16 unused).
-cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* k16, const void* v16,
-                              bool bf16, const void* split, cudaStream_t st);
+// q16: the prepared query rows [S][H][hd] in the MMA operand type (RMSNorm +
+// RoPE already applied by launch_prep_kv), or their f16 hi/lo planes when
+// split. k16/v16: 16-bit K/V rows [S][Hkv][hd] (the cache when it is
+// f16/bf16). split: f16 hi/lo K/V planes when the cache is f32 (k16/v16
+// unused then).
+cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* q16, const void* k16,
+                              const void* v16, bool bf16, const void* split, cudaStream_t st);
 bool prefill_tc_supported(int hd);
 
 }  // namespace eb

@@ -4,21 +4,26 @@
 // :94-120): o[i,h] = softmax_j<=i(scale * q[i,h] . k[j,kvh]) v[j,kvh], with
 // kvh = h / (H/Hkv), seq-major layouts.
 //
-// One CTA = one 128-row query tile of one query head (256 threads):
-//   warp 0      TMA producer: K/V tiles [BN rows x 64 dims] (128-byte swizzle)
-//               into an NST-deep shared-memory ring.
-//   warp 1      TMEM owner + MMA issuer (one thread): S = Q K^T into TMEM,
-//               then O += P V into TMEM.
-//   warps 4..7  one thread per query row: load the q row, RMSNorm + RoPE it
-//               in registers, write it as the swizzled MMA operand; per KV
-//               tile read the S row from TMEM, online softmax in f32 (exp2),
-//               rescale the O row in TMEM when the max moves, write P (16-bit)
-//               as the operand of the PV MMA; finally O / l to global memory.
+// One CTA = NQ query tiles of 128 rows (the two heads of a GQA pair when the
+// group size is even, so each K/V tile feeds twice the MMA work):
+//   warp 0      TMA producer: the query tiles (already normalised, rotated and
+//               rounded to the operand type by the row-prep pass), then K and
+//               V tiles [BN rows x 64 dims] (128-byte swizzle) into separate
+//               NSTK- and NSTV-deep shared-memory rings.
+//   warp 1      TMEM owner + MMA issuer (one thread): S_t = Q_t K^T into TMEM,
+//               then O_t += P_t V with P read from TMEM (it overwrites S_t).
+//   warps 2-3   idle (softmax warps must start at a multiple of 4: a warp may
+//               only address TMEM lanes 32*(warp%4)..+31).
+//   warps 4..   one thread per query row of each tile: per KV tile read the S
+//               row from TMEM, online softmax in f32 (exp2 on MUFU, some
+//               column pairs on the FMA pipe), rescale the O row in TMEM when
+//               the max moves past a threshold, write P (16-bit) back over S;
+//               finally O / l to global memory.
 // K/V come from the cache the K/V preparation pass has just written (the
 // reference attends the same post-RoPE k / post-norm v it writes,
 // crates/eyebrowse-nn/src/attention.rs:78-115).
 //
-// f32 inputs (SPLIT): every operand x is carried as two f16 values
+// f32 caches (SPLIT): every operand x is carried as two f16 values
 // hi = f16(x), lo = f16(x - hi); S = Qh.Kh + Qh.Kl + Ql.Kh and
 // O += Ph.Vh + Ph.Vl + Pl.Vh (the standard error-compensated split, which
 // keeps ~21 mantissa bits on f16 tensor cores).
@@ -33,7 +38,10 @@
 
 namespace eb {
 
-
+#ifndef EB_PREFILL_EMU_PAIRS
+#define EB_PREFILL_EMU_PAIRS 2
+#endif
+constexpr int kEmuPairsOf8 = EB_PREFILL_EMU_PAIRS;
 
 // Tile geometry. NQ query tiles (heads of one GQA group, same rows) share
 // each K/V tile. NSB S buffers per query tile: with one query tile, two S
@@ -57,6 +65,10 @@ struct PfCfg {
   static constexpr int S_COL0 = NQ * HD;
   static constexpr int TMEM_COLS = constexpr_pow2ceil(S_COL0 + NQ * NSB * BN);
   static constexpr int THREADS = 128 + 128 * NQ;
+  // Of every 8 column pairs of P, this many take their exp2 on the FMA pipe
+  // (ex2_fma_pair) and the rest on MUFU. The hi/lo split path keeps MUFU for
+  // all: its P carries ~21 bits, beyond the polynomial's accuracy.
+  static constexpr int EMU_PAIRS = SPLIT ? 0 : kEmuPairsOf8;
   static_assert(HD % 64 == 0 && HD <= 256, "head_dim");
   static_assert(BN % 32 == 0 && BN <= 128, "kv tile");
   static_assert(TMEM_COLS <= 512, "tensor memory budget");
@@ -70,7 +82,9 @@ enum { kBarQ = 0, kBarFinal = 1, kBarS0 = 2 };
 
 template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV>
 __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                      const __grid_constant__ CUtensorMap tmQlo,
+                      const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV,
                       const __grid_constant__ CUtensorMap tmKlo,
                       const __grid_constant__ CUtensorMap tmVlo, PrefillArgs a) {
@@ -107,7 +121,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
   const int n_tiles = (kv_rows + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(kBarQ), 128 * NQ);
+    mbar_init(bar(kBarQ), 1);
     mbar_init(bar(kBarFinal), 1);
     for (int i = kSFull0; i < kPFull0; i++) mbar_init(bar(i), 1);
     for (int i = kPFull0; i < kODone0; i++) mbar_init(bar(i), 128);
@@ -117,9 +131,11 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     fence_async_smem();
   }
   if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmQ);
     tma_prefetch_map(&tmK);
     tma_prefetch_map(&tmV);
     if (SPLIT) {
+      tma_prefetch_map(&tmQlo);
       tma_prefetch_map(&tmKlo);
       tma_prefetch_map(&tmVlo);
     }
@@ -140,6 +156,17 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     // K gets the deeper ring: K_{j+1} is needed one step after K_{j+1-NSTK}
     // frees, V_{j+1} two steps after V_{j+1-NSTV}.
     if (lane == 0) {
+      // The query tiles (rows past S read as zeros): NQ heads x HB boxes of
+      // [128 rows x 64 dims], hi and lo planes when split.
+      mbar_arrive_expect_tx(bar(kBarQ), C::Q_BYTES);
+#pragma unroll
+      for (int t = 0; t < NQ; t++)
+#pragma unroll
+        for (int hb = 0; hb < C::HB; hb++) {
+          const uint32_t dst = sQ + t * C::QT_BYTES + hb * C::TILE128;
+          tma_load_3d(dst, &tmQ, bar(kBarQ), hb * 64, grp * NQ + t, q0);
+          if (SPLIT) tma_load_3d(dst + C::HB * C::TILE128, &tmQlo, bar(kBarQ), hb * 64, grp * NQ + t, q0);
+        }
       int kiss[NSTK], viss[NSTV];
       for (int s = 0; s < NSTK; s++) kiss[s] = 0;
       for (int s = 0; s < NSTV; s++) viss[s] = 0;
@@ -171,6 +198,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         viss[sv]++;
       }
       // Every issued copy has landed before the CTA can exit.
+      mbar_drain(bar(kBarQ), 0, a.err, kErrTimeoutTma);
       for (int s = 0; s < NSTK; s++)
         if (kiss[s]) mbar_drain(bar(kKFull0 + s), (kiss[s] - 1) & 1, a.err, kErrTimeoutTma);
       for (int s = 0; s < NSTV; s++)
@@ -291,92 +319,6 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     const int q_row = q0 + r;
     const bool valid = q_row < a.S;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t qtile = sQ + t * C::QT_BYTES;
-    // Q row: RMSNorm (pass 1: sum of squares), then norm + RoPE per 8-wide
-    // chunk pair (p, p + HD/2) straight into the swizzled operand.
-    {
-      const int64_t qbase = (int64_t)q_row * a.q_stride + (int64_t)h * HD;
-      float inv = 1.f;
-      if (valid && a.q_norm_w) {
-        float ss = 0.f;
-        for (int d = 0; d < HD; d += 8) {
-          float f[8];
-          load8_any(a.q, qbase + d, a.dtype_q, f);
-#pragma unroll
-          for (int i = 0; i < 8; i++) ss = __fadd_rn(ss, __fmul_rn(f[i], f[i]));
-        }
-        inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
-      }
-      const float* crow = a.cos_t ? a.cos_t + (int64_t)q_row * (HD / 2) : nullptr;
-      const float* srow = a.sin_t ? a.sin_t + (int64_t)q_row * (HD / 2) : nullptr;
-      // QB rotation pairs per batch: every global load of a batch is issued
-      // before its shared-memory stores (which the compiler will not cross).
-      constexpr int QB = (NQ == 2 || HD / 2 < 32) ? 16 : 32;
-#pragma unroll 1
-      for (int pb = 0; pb < HD / 2; pb += QB) {
-        float x1[QB], x2[QB];
-        if (valid) {
-#pragma unroll
-          for (int u = 0; u < QB; u += 8) {
-            float f1[8], f2[8];
-            load8_any(a.q, qbase + pb + u, a.dtype_q, f1);
-            load8_any(a.q, qbase + HD / 2 + pb + u, a.dtype_q, f2);
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-              x1[u + i] = f1[i];
-              x2[u + i] = f2[i];
-            }
-          }
-          if (a.q_norm_w) {
-#pragma unroll
-            for (int i = 0; i < QB; i++) {
-              x1[i] = __fmul_rn(__fmul_rn(x1[i], inv), a.q_norm_w[pb + i]);
-              x2[i] = __fmul_rn(__fmul_rn(x2[i], inv), a.q_norm_w[HD / 2 + pb + i]);
-            }
-          }
-          if (crow) {
-#pragma unroll
-            for (int i = 0; i < QB; i += 4) {
-              const float4 c4 = *reinterpret_cast<const float4*>(crow + pb + i);
-              const float4 s4 = *reinterpret_cast<const float4*>(srow + pb + i);
-              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int e = 0; e < 4; e++) {
-                const float y1 = __fsub_rn(__fmul_rn(x1[i + e], cc[e]), __fmul_rn(x2[i + e], ss[e]));
-                const float y2 = __fadd_rn(__fmul_rn(x2[i + e], cc[e]), __fmul_rn(x1[i + e], ss[e]));
-                x1[i + e] = y1;
-                x2[i + e] = y2;
-              }
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < QB; i++) x1[i] = x2[i] = 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < QB; u += 8) {
-          float f1[8], f2[8];
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-            f1[i] = x1[u + i];
-            f2[i] = x2[u + i];
-          }
-          const int c1 = (pb + u) / 8, c2 = (HD / 2 + pb + u) / 8;
-          const uint32_t a1 = qtile + (c1 >> 3) * C::TILE128 + sw128_offset(r, c1 & 7);
-          const uint32_t a2 = qtile + (c2 >> 3) * C::TILE128 + sw128_offset(r, c2 & 7);
-          if (SPLIT) {
-            st_chunk_split(a1, a1 + C::HB * C::TILE128, f1);
-            st_chunk_split(a2, a2 + C::HB * C::TILE128, f2);
-          } else {
-            st_chunk<BF16>(a1, f1);
-            st_chunk<BF16>(a2, f2);
-          }
-        }
-      }
-      fence_async_smem();
-      mbar_arrive(bar(kBarQ));
-    }
-
     const float sl2 = a.scale_log2;
     const uint32_t tO = tmem + lane_off + t * HD;
     float m_run = -INFINITY, l_run = 0.f;
@@ -456,10 +398,10 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
       // pass 2: re-read S in halves, P = exp2(s*scale - m) -> 16-bit operand in
       // TMEM over the columns already consumed (P half h lands in S columns
       // [h*HALF/2, (h+1)*HALF/2), which this pass has read before)
-      const float neg_m = -m_run;
-      float rsum[8];
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m_run, -m_run);
+      uint64_t rsum2[4];
 #pragma unroll
-      for (int i = 0; i < 8; i++) rsum[i] = 0.f;
+      for (int i = 0; i < 4; i++) rsum2[i] = 0;
       constexpr int HALF = BN >= 64 ? 64 : BN;
 #pragma unroll
       for (int hbase = 0; hbase < BN; hbase += HALF) {
@@ -482,9 +424,15 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         uint32_t pl[SPLIT ? HALF / 2 : 1];
 #pragma unroll
         for (int c = 0; c < HALF; c += 2) {
-          const float p0 = ex2(fmaf(x[c], sl2, neg_m));
-          const float p1 = ex2(fmaf(x[c + 1], sl2, neg_m));
-          rsum[(c >> 1) & 7] += p0 + p1;
+          float y0, y1, p0, p1;
+          f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sl2x2, negm2), y0, y1);
+          if (((c >> 1) & 7) < C::EMU_PAIRS) {
+            ex2_fma_pair(y0, y1, p0, p1);
+          } else {
+            p0 = ex2(y0);
+            p1 = ex2(y1);
+          }
+          rsum2[(c >> 1) & 3] = f2_add(rsum2[(c >> 1) & 3], f2_pack(p0, p1));
           if (SPLIT) {
             const __half2 hh = __floats2half2_rn(p0, p1);
             const float2 hf = __half22float2(hh);
@@ -523,8 +471,12 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
                 : "memory");
         }
       }
-      l_run += ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) +
-               ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
+      {
+        float rs[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) f2_unpack(rsum2[i], rs[2 * i], rs[2 * i + 1]);
+        l_run += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+      }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar(kPFull0 + t));
@@ -613,8 +565,8 @@ bool make_kv_map(CUtensorMap* m, const void* base, int S, int Hkv, int hd, int B
 }
 
 template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV>
-static cudaError_t run_prefill(const PrefillArgs& a, const void* k16, const void* v16,
-                               const void* split, cudaStream_t st) {
+static cudaError_t run_prefill(const PrefillArgs& a, const void* q16, const void* k16,
+                               const void* v16, const void* split, cudaStream_t st) {
   using C = PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>;
   auto kern = prefill_tc_kernel<HD, BN, NQ, SPLIT, BF16, NSTK, NSTV>;
   static unsigned configured = 0;  // one bit per device
@@ -626,7 +578,16 @@ static cudaError_t run_prefill(const PrefillArgs& a, const void* k16, const void
     if (e != cudaSuccess) return e;
     __atomic_fetch_or(&configured, 1u << (dev & 31), __ATOMIC_RELEASE);
   }
-  CUtensorMap mk, mv, mkl, mvl;
+  CUtensorMap mq, mql, mk, mv, mkl, mvl;
+  if (SPLIT) {
+    const __half* qp = reinterpret_cast<const __half*>(q16);
+    if (!make_kv_map(&mq, qp, a.S, a.H, HD, 128, false) ||
+        !make_kv_map(&mql, qp + (size_t)a.S * a.H * HD, a.S, a.H, HD, 128, false))
+      return cudaErrorInvalidValue;
+  } else {
+    if (!make_kv_map(&mq, q16, a.S, a.H, HD, 128, BF16)) return cudaErrorInvalidValue;
+    mql = mq;
+  }
   if (SPLIT) {
     const size_t plane = (size_t)a.S * a.Hkv * HD;
     const __half* sp = reinterpret_cast<const __half*>(split);
@@ -643,42 +604,42 @@ static cudaError_t run_prefill(const PrefillArgs& a, const void* k16, const void
     mvl = mv;
   }
   const int n_qt = (a.S + 127) / 128;
-  kern<<<(unsigned)(n_qt * (a.H / NQ)), C::THREADS, C::SMEM, st>>>(mk, mv, mkl, mvl, a);
+  kern<<<(unsigned)(n_qt * (a.H / NQ)), C::THREADS, C::SMEM, st>>>(mq, mql, mk, mv, mkl, mvl, a);
   return cudaGetLastError();
 }
 
 bool prefill_tc_supported(int hd) { return hd == 64 || hd == 128 || hd == 256; }
 
-cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* k16, const void* v16,
-                              bool bf16, const void* split, cudaStream_t st) {
+cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* q16, const void* k16,
+                              const void* v16, bool bf16, const void* split, cudaStream_t st) {
   // Two query tiles per CTA when the heads of a GQA group pair up.
   const bool pair = ((a.H / a.Hkv) % 2) == 0;
   if (split) {
     switch (hd) {
       case 64:
-        return run_prefill<64, 128, 1, true, false, 2, 2>(a, k16, v16, split, st);
-      case 128: return run_prefill<128, 64, 1, true, false, 2, 2>(a, k16, v16, split, st);
-      case 256: return run_prefill<256, 32, 1, true, false, 1, 1>(a, k16, v16, split, st);
+        return run_prefill<64, 128, 1, true, false, 2, 2>(a, q16, k16, v16, split, st);
+      case 128: return run_prefill<128, 64, 1, true, false, 2, 2>(a, q16, k16, v16, split, st);
+      case 256: return run_prefill<256, 32, 1, true, false, 1, 1>(a, q16, k16, v16, split, st);
     }
   } else if (bf16) {
     switch (hd) {
       case 64:
-        return pair ? run_prefill<64, 128, 2, false, true, 4, 3>(a, k16, v16, split, st)
-                    : run_prefill<64, 128, 1, false, true, 4, 3>(a, k16, v16, split, st);
+        return pair ? run_prefill<64, 128, 2, false, true, 4, 3>(a, q16, k16, v16, split, st)
+                    : run_prefill<64, 128, 1, false, true, 4, 3>(a, q16, k16, v16, split, st);
       case 128:
-        return pair ? run_prefill<128, 128, 2, false, true, 3, 2>(a, k16, v16, split, st)
-                    : run_prefill<128, 128, 1, false, true, 3, 2>(a, k16, v16, split, st);
-      case 256: return run_prefill<256, 64, 1, false, true, 2, 2>(a, k16, v16, split, st);
+        return pair ? run_prefill<128, 128, 2, false, true, 3, 2>(a, q16, k16, v16, split, st)
+                    : run_prefill<128, 128, 1, false, true, 3, 2>(a, q16, k16, v16, split, st);
+      case 256: return run_prefill<256, 64, 1, false, true, 2, 2>(a, q16, k16, v16, split, st);
     }
   } else {
     switch (hd) {
       case 64:
-        return pair ? run_prefill<64, 128, 2, false, false, 4, 3>(a, k16, v16, split, st)
-                    : run_prefill<64, 128, 1, false, false, 4, 3>(a, k16, v16, split, st);
+        return pair ? run_prefill<64, 128, 2, false, false, 4, 3>(a, q16, k16, v16, split, st)
+                    : run_prefill<64, 128, 1, false, false, 4, 3>(a, q16, k16, v16, split, st);
       case 128:
-        return pair ? run_prefill<128, 128, 2, false, false, 3, 2>(a, k16, v16, split, st)
-                    : run_prefill<128, 128, 1, false, false, 3, 2>(a, k16, v16, split, st);
-      case 256: return run_prefill<256, 64, 1, false, false, 2, 2>(a, k16, v16, split, st);
+        return pair ? run_prefill<128, 128, 2, false, false, 3, 2>(a, q16, k16, v16, split, st)
+                    : run_prefill<128, 128, 1, false, false, 3, 2>(a, q16, k16, v16, split, st);
+      case 256: return run_prefill<256, 64, 1, false, false, 2, 2>(a, q16, k16, v16, split, st);
     }
   }
   return cudaErrorNotSupported;

@@ -161,13 +161,14 @@ constexpr int kPrepWarps = 4;
 __global__ void __launch_bounds__(kPrepWarps * 32) prep_kv_kernel(PrepArgs a) {
   __shared__ float buf[kPrepWarps][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t per_seq = (int64_t)a.rows * a.hkv * 2;
+  const int nk = a.v ? 2 : 1;  // k and v rows, or k rows only
+  const int64_t per_seq = (int64_t)a.rows * a.hkv * nk;
   const int64_t task = blockIdx.x * (int64_t)kPrepWarps + warp;
   if (task >= per_seq * a.batch) return;
   const int b = (int)(task / per_seq);
   int64_t t = task % per_seq;
-  const int which = (int)(t & 1);  // 0 = k, 1 = v
-  t >>= 1;
+  const int which = nk == 2 ? (int)(t & 1) : 0;  // 0 = k, 1 = v
+  t >>= (nk - 1);
   const int head = (int)(t % a.hkv);
   const int r = (int)(t / a.hkv);
   const int hd = a.hd;
@@ -202,81 +203,165 @@ __global__ void __launch_bounds__(kPrepWarps * 32) prep_kv_kernel(PrepArgs a) {
   }
 }
 
-// Vectorised K/V prep for head_dim = 32*E (64/128/256): RPW rows per warp,
-// all loads issued before any math (row helpers in eb_rowops.cuh).
-template <int E>
-__global__ void __launch_bounds__(256) prep_kv_vec_kernel(PrepArgs a) {
-  constexpr int HD = 32 * E;
-  constexpr int RPW = 4;
+// Row prep for head_dim 64/128/256 with inputs of ES bytes per element: one
+// warp takes HPW consecutive heads of one token row of k (or v), which are
+// contiguous in memory. A lane owns 8 consecutive elements of a head row
+// (16-byte loads for 16-bit inputs), LPR = HD/8 lanes share a head row, and
+// all of the warp's loads (HPW head rows, one RoPE table row, this lane's
+// norm weights) are in flight together. The RMSNorm sum of squares is a
+// butterfly over the row's lanes; the RoPE partner chunk (HD/2 elements
+// away) is LPR/2 lanes away. Per-element arithmetic as in warp_kv_row.
+template <int HD, int HPW, int ES>
+__global__ void __launch_bounds__(128) prep_rows_kernel(PrepArgs a) {
+  constexpr int LPR = HD / 8;            // lanes per head row
+  constexpr int RPI = 32 / LPR;          // head rows per warp instruction
+  constexpr int NI = (HPW + RPI - 1) / RPI;
+  constexpr int NW = ES == 4 ? 2 : 1;    // 16-byte words per lane per head row
   const int lane = threadIdx.x & 31;
   const int64_t warp_id = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-  const int64_t per_seq = (int64_t)a.rows * a.hkv * 2;
-  const int64_t total = per_seq * a.batch;
-  float x[RPW][E];
-  int64_t task[RPW];
+  const int nk = a.v ? 2 : 1;  // k and v rows, or k rows only
+  const int n_g = a.hkv / HPW;
+  const int per_seq = a.rows * n_g * nk;
+  if (warp_id >= (int64_t)per_seq * a.batch) return;
+  const int b = (int)(warp_id / per_seq);
+  int rem = (int)(warp_id - (int64_t)b * per_seq);
+  const int which = nk == 2 ? (rem & 1) : 0;
+  rem >>= (nk - 1);
+  const int g = rem % n_g;
+  const int r = rem / n_g;
+  const int pos = (a.positions ? a.positions[b] : a.pos0) + r;
+  const int c8 = (lane % LPR) * 8;
+  const int hsub = lane / LPR;
+  const void* src = which ? a.v : a.k;
+  const int64_t base = b * a.kv_bstride + (int64_t)r * a.kv_stride + (int64_t)g * HPW * HD + c8;
+  uint4 raw[NI][NW];
 #pragma unroll
-  for (int i = 0; i < RPW; i++) {
-    task[i] = warp_id * RPW + i;
-    if (task[i] < total) {
-      const int64_t b = task[i] / per_seq;
-      int64_t t = task[i] % per_seq;
-      const int which = (int)(t & 1);
-      t >>= 1;
-      const int head = (int)(t % a.hkv);
-      const int r = (int)(t / a.hkv);
-      ld_row<E>(which ? a.v : a.k,
-                b * a.kv_bstride + (int64_t)r * a.kv_stride + (int64_t)head * HD + lane * E,
-                a.dtype_kv, x[i]);
+  for (int i = 0; i < NI; i++) {
+    if (i * RPI + hsub < HPW) {
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const char*>(src) +
+                                                      (base + (int64_t)(i * RPI + hsub) * HD) * ES);
+#pragma unroll
+      for (int w = 0; w < NW; w++) raw[i][w] = p[w];
     }
   }
+  const float* wn = which ? a.v_norm_w : a.k_norm_w;
+  float wt[8], cs[8], sn[8];
+  if (wn) {
+    const float4 w0 = *reinterpret_cast<const float4*>(wn + c8);
+    const float4 w1 = *reinterpret_cast<const float4*>(wn + c8 + 4);
+    wt[0] = w0.x; wt[1] = w0.y; wt[2] = w0.z; wt[3] = w0.w;
+    wt[4] = w1.x; wt[5] = w1.y; wt[6] = w1.z; wt[7] = w1.w;
+  }
+  const bool rope = !which && a.cos_t;
+  if (rope) {
+    const int64_t off = (int64_t)pos * (HD / 2) + (c8 % (HD / 2));
+    const float4 c0 = *reinterpret_cast<const float4*>(a.cos_t + off);
+    const float4 c1 = *reinterpret_cast<const float4*>(a.cos_t + off + 4);
+    const float4 s0 = *reinterpret_cast<const float4*>(a.sin_t + off);
+    const float4 s1 = *reinterpret_cast<const float4*>(a.sin_t + off + 4);
+    cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
+    cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+    sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+    sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+  }
+  const bool first_half = c8 < HD / 2;
+  void* cache = which ? a.vcache : a.kcache;
 #pragma unroll
-  for (int i = 0; i < RPW; i++) {
-    if (task[i] >= total) break;
-    const int64_t b = task[i] / per_seq;
-    int64_t t = task[i] % per_seq;
-    const int which = (int)(t & 1);
-    t >>= 1;
-    const int head = (int)(t % a.hkv);
-    const int r = (int)(t / a.hkv);
-    const int pos = (a.positions ? a.positions[b] : a.pos0) + r;
-    float* v = x[i];
-    warp_kv_row<E>(x[i], which ? a.v_norm_w : a.k_norm_w, a.eps,
-                   (!which && a.cos_t) ? a.cos_t + (int64_t)pos * (HD / 2) : nullptr,
-                   (!which && a.cos_t) ? a.sin_t + (int64_t)pos * (HD / 2) : nullptr, lane);
+  for (int i = 0; i < NI; i++) {
+    const int hl = i * RPI + hsub;  // head within the group (lanes past HPW idle)
+    float x[8];
+    if (ES == 4) {
+      const float* f = reinterpret_cast<const float*>(&raw[i][0]);
 #pragma unroll
-    for (int e = 0; e < E; e++) v[e] = round_to(v[e], a.dtype_cache);
-    void* cache = which ? a.vcache : a.kcache;
+      for (int k = 0; k < 8; k++) x[k] = f[k];
+    } else {
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&raw[i][0]);
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        float2 t;
+        if (a.dtype_kv == kF16) t = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
+        else t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[k]));
+        x[2 * k] = t.x;
+        x[2 * k + 1] = t.y;
+      }
+    }
+    if (hl >= HPW) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) x[k] = 0.f;
+    }
+    if (wn) {
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; k++) ss = __fadd_rn(ss, __fmul_rn(x[k], x[k]));
+#pragma unroll
+      for (int off = 1; off < LPR; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      const float inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+#pragma unroll
+      for (int k = 0; k < 8; k++) x[k] = __fmul_rn(__fmul_rn(x[k], inv), wt[k]);
+    }
+    if (rope) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const float o = __shfl_xor_sync(0xffffffffu, x[k], LPR / 2);
+        x[k] = first_half ? __fsub_rn(__fmul_rn(x[k], cs[k]), __fmul_rn(o, sn[k]))
+                          : __fadd_rn(__fmul_rn(x[k], cs[k]), __fmul_rn(o, sn[k]));
+      }
+    }
+    if (hl >= HPW) continue;
+    const int head = g * HPW + hl;
+#pragma unroll
+    for (int k = 0; k < 8; k++) x[k] = round_to(x[k], a.dtype_cache);
     if (cache)
-      st_row<E>(cache, b * a.cache_bstride + ((int64_t)pos * a.hkv + head) * HD + lane * E,
-                a.dtype_cache, x[i]);
+      st_row<8>(cache, b * a.cache_bstride + ((int64_t)pos * a.hkv + head) * HD + c8,
+                a.dtype_cache, x);
     if (a.split) {
       const int64_t plane = (int64_t)a.rows * a.hkv * HD;
       __half* hi = reinterpret_cast<__half*>(a.split) + (which ? 2 * plane : 0);
-      float fh[E], fl[E];
+      float fh[8], fl[8];
 #pragma unroll
-      for (int e = 0; e < E; e++) {
-        fh[e] = __half2float(__float2half_rn(v[e]));
-        fl[e] = v[e] - fh[e];
+      for (int k = 0; k < 8; k++) {
+        fh[k] = __half2float(__float2half_rn(x[k]));
+        fl[k] = x[k] - fh[k];
       }
-      const int64_t srow = ((int64_t)r * a.hkv + head) * HD + lane * E;
-      st_row<E>(hi, srow, kF16, fh);
-      st_row<E>(hi + plane, srow, kF16, fl);
+      const int64_t srow = ((int64_t)r * a.hkv + head) * HD + c8;
+      st_row<8>(hi, srow, kF16, fh);
+      st_row<8>(hi + plane, srow, kF16, fl);
     }
   }
 }
 
+template <int HD, int ES>
+static void launch_prep_rows(const PrepArgs& a, int hpw, cudaStream_t st) {
+  const int64_t warps = (int64_t)a.rows * (a.hkv / hpw) * (a.v ? 2 : 1) * a.batch;
+  const unsigned blocks = (unsigned)((warps + 3) / 4);
+  switch (hpw) {
+    case 16: prep_rows_kernel<HD, 16, ES><<<blocks, 128, 0, st>>>(a); break;
+    case 8: prep_rows_kernel<HD, 8, ES><<<blocks, 128, 0, st>>>(a); break;
+    case 4: prep_rows_kernel<HD, 4, ES><<<blocks, 128, 0, st>>>(a); break;
+    case 2: prep_rows_kernel<HD, 2, ES><<<blocks, 128, 0, st>>>(a); break;
+    default: prep_rows_kernel<HD, 1, ES><<<blocks, 128, 0, st>>>(a); break;
+  }
+}
+
 cudaError_t launch_prep_kv(const PrepArgs& a, cudaStream_t st) {
-  const int64_t tasks = (int64_t)a.rows * a.hkv * 2 * a.batch;
+  const int64_t tasks = (int64_t)a.rows * a.hkv * (a.v ? 2 : 1) * a.batch;
   if (tasks == 0) return cudaSuccess;
   const int es_in = a.dtype_kv == kF32 ? 4 : 2;
+  const int es_c = a.dtype_cache == kF32 ? 4 : 2;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   const bool aligned = ((a.kv_stride * es_in) % 16 == 0) && ((a.kv_bstride * es_in) % 16 == 0) &&
-                       ((reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v)) & 15) == 0;
+                       ((a.cache_bstride * es_c) % 16 == 0) && al16(a.k) && al16(a.v) &&
+                       al16(a.kcache) && al16(a.vcache) && al16(a.split) &&
+                       ((a.cos_t == nullptr) || (al16(a.cos_t) && al16(a.sin_t))) &&
+                       al16(a.k_norm_w) && al16(a.v_norm_w);
   if (aligned && (a.hd == 64 || a.hd == 128 || a.hd == 256)) {
-    const int64_t warps = (tasks + 3) / 4;
-    const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
-    if (a.hd == 64) prep_kv_vec_kernel<2><<<blocks, 256, 0, st>>>(a);
-    else if (a.hd == 128) prep_kv_vec_kernel<4><<<blocks, 256, 0, st>>>(a);
-    else prep_kv_vec_kernel<8><<<blocks, 256, 0, st>>>(a);
+    // heads per warp: the largest power of two up to 16 (8 for head_dim 256)
+    // that divides the head count
+    int hpw = a.hd == 256 ? 8 : 16;
+    while (a.hkv % hpw) hpw >>= 1;
+    if (a.hd == 64) es_in == 4 ? launch_prep_rows<64, 4>(a, hpw, st) : launch_prep_rows<64, 2>(a, hpw, st);
+    else if (a.hd == 128) es_in == 4 ? launch_prep_rows<128, 4>(a, hpw, st) : launch_prep_rows<128, 2>(a, hpw, st);
+    else es_in == 4 ? launch_prep_rows<256, 4>(a, hpw, st) : launch_prep_rows<256, 2>(a, hpw, st);
     return cudaGetLastError();
   }
   prep_kv_kernel<<<(unsigned)((tasks + kPrepWarps - 1) / kPrepWarps), kPrepWarps * 32, 0, st>>>(a);

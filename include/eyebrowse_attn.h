@@ -62,8 +62,9 @@ EB_API const char* eb_version(void);
 /* Causal GQA attention over full sequences, q [s,h,hd], k/v [s,hkv,hd] -> o [s,h,hd].
  * Replaces attn_prefill (crates/eyebrowse-kernels/src/attention.rs:94-120).
  * head_dim 64/128/256 runs on tcgen05 tensor cores (f32 operands split into
- * f16 hi/lo pairs; needs eb_attn_prefill_workspace_bytes of workspace); other
- * even head_dim up to 256 run a SIMT kernel and need no workspace. */
+ * f16 hi/lo pairs, staged with the q rows in eb_attn_prefill_workspace_bytes
+ * of workspace); other even head_dim up to 256 run a SIMT kernel and need no
+ * workspace. */
 EB_API int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, int64_t h,
                     int64_t hkv, int64_t s, int64_t hd, float scale, void* workspace,
                     size_t workspace_bytes, eb_stream_t stream);
@@ -135,7 +136,9 @@ typedef struct {
 /* Prefill of `seq` rows at positions 0..seq-1 (Attention::prefill,
  * crates/eyebrowse-nn/src/attention.rs:49-117): normalises and rotates q/k,
  * normalises v, writes k/v to cache rows [0, seq) and computes causal GQA
- * attention into o [seq, n_heads, head_dim]. */
+ * attention into o [seq, n_heads, head_dim]. head_dim 64/128/256 (tensor
+ * cores) stage the prepared q rows, and the f16 hi/lo planes of an f32
+ * cache, in eb_attention_prefill_workspace_bytes of workspace. */
 EB_API int eb_attention_prefill(const eb_attn_desc* desc, const eb_attn_layer* layer, int64_t seq,
                          const void* q, const void* k, const void* v, void* kcache,
                          void* vcache, void* o, void* workspace, size_t workspace_bytes,
@@ -147,8 +150,8 @@ EB_API size_t eb_attention_prefill_workspace_bytes(const eb_attn_desc* desc, int
  * workspace).
  * _kv: k -> RMSNorm -> RoPE, v -> RMSNorm, written to cache rows [0, seq)
  * (Attention::prefill's norms, rope and kv_write, attention.rs:62-97).
- * _attend: q -> RMSNorm -> RoPE fused into the causal attention over cache
- * rows [0, seq) (attention.rs:62-76, :104-115). */
+ * _attend: q -> RMSNorm -> RoPE (a row pass into the workspace), then the
+ * causal attention over cache rows [0, seq) (attention.rs:62-76, :104-115). */
 EB_API int eb_attention_prefill_kv(const eb_attn_desc* desc, const eb_attn_layer* layer,
                                    int64_t seq, const void* k, const void* v, void* kcache,
                                    void* vcache, void* workspace, size_t workspace_bytes,

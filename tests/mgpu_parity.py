@@ -48,8 +48,9 @@ def main() -> int:
     kc = torch.empty(S, sh.n_kv_heads, hd, device="cuda", dtype=f16)
     vc = torch.empty_like(kc)
     o = torch.empty(S, sh.n_heads, hd, device="cuda", dtype=f16)
+    ws = eb.alloc_workspace(eb.attention_prefill_workspace_bytes(desc, S))
     eb.attention_prefill(desc, layer, S, dev(q[:, sh.h0:sh.h1]), dev(k[:, sh.kv0:sh.kv1]),
-                         dev(v[:, sh.kv0:sh.kv1]), kc, vc, o, None)
+                         dev(v[:, sh.kv0:sh.kv1]), kc, vc, o, ws)
     gath = torch.empty(world, S, sh.n_heads, hd, device="cuda", dtype=f16)
     full = torch.empty(S, H, hd, device="cuda", dtype=f16)
     gather_heads(o, gath, full, world, S, sh.n_heads, hd, eb.EB_F16)

@@ -77,7 +77,11 @@ def test_workspace_sizes(eb):
     b = eb.attention_decode_workspace_bytes(d, 64, 32767)
     assert a > 0 and b > a and a % 256 == 0
     assert eb.attention_decode_workspace_bytes(d, 1, 10) == 0  # short context: one CTA per head
-    assert eb.attn_prefill_workspace_bytes(16, 8, 128, 128) == 4 * 128 * 8 * 128 * 2
+    # f16 hi/lo planes of k and v, then of the prepared q rows
+    assert eb.attn_prefill_workspace_bytes(16, 8, 128, 128) == (4 * 128 * 8 + 2 * 128 * 16) * 128 * 2
     assert eb.attn_prefill_workspace_bytes(2, 1, 5, 8) == 0  # SIMT path
     f16 = eb.make_desc(32, 8, 128, 8192, dtype_qkv=eb.EB_F16, dtype_cache=eb.EB_F16)
-    assert eb.attention_prefill_workspace_bytes(f16, 8192) == 0  # reads the f16 cache directly
+    # reads the f16 cache directly; stages only the prepared f16 q rows
+    assert eb.attention_prefill_workspace_bytes(f16, 8192) == 8192 * 32 * 128 * 2
+    odd = eb.make_desc(4, 2, 96, 64, dtype_qkv=eb.EB_F16, dtype_cache=eb.EB_F16)
+    assert eb.attention_prefill_workspace_bytes(odd, 64) == 0  # SIMT path

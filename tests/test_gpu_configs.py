@@ -87,8 +87,9 @@ def test_config3_prefill_llama3_f16(eb, orc, S):
     kc = torch.zeros(max_seq * Hkv * hd, device="cuda", dtype=torch.float16)
     vc = torch.zeros_like(kc)
     o = torch.empty(S * H * hd, device="cuda", dtype=torch.float16)
+    ws = eb.alloc_workspace(eb.attention_prefill_workspace_bytes(desc, S))
     eb.attention_prefill(desc, layer, S, to_dev(q, torch.float16), to_dev(k, torch.float16),
-                         to_dev(v, torch.float16), kc, vc, o, None)
+                         to_dev(v, torch.float16), kc, vc, o, ws)
     # oracle inputs: the post-RoPE q/k rounded to f16 as the kernel stores/feeds them
     qr = orc.round_f16(orc.rope(q, cos, sin, S, H, hd))
     kr = orc.round_f16(orc.rope(k, cos, sin, S, Hkv, hd))
