@@ -37,6 +37,9 @@ from eyebrowse_b200.sharded import gather_heads, head_shard  # noqa: E402
 
 METRIC = "prefill attn TFLOP/s & decode KV GB/s at 1/2/4/8 B200 vs roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# Untimed seconds before each timed loop: long enough for the SM clock to
+# settle under the 1000 W power cap, so the timed region sees steady clocks.
+WARM_S = 1.5
 
 
 def load_peaks():
@@ -67,28 +70,72 @@ def profile_traffic(key: str):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples of this GPU's clocks and throttle reasons."""
+    """This GPU's SM clock and clock-event reasons, sampled every few ms while a
+    timed region runs: NVML polled from a thread (nvidia_ml_py), else
+    `nvidia-smi -lms` as a fallback. Only samples inside the marked region are
+    summarised."""
 
     FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, uuid: str | None, period_ms: int = 25):
+    def __init__(self, uuid: str | None, period_ms: int = 5):
         self.uuid = uuid
-        self.samples = []  # (t, sm, max, reasons:set)
+        self.samples = []  # (t, sm, max, reasons:set, watts)
         self.proc = None
         self.period_ms = period_ms
         self.t_lo = self.t_hi = None
+        self._stop = threading.Event()
+        self.source = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        want = (self.uuid or "").lower().replace("gpu-", "")
+        for i in range(pynvml.nvmlDeviceGetCount()):
+            h = pynvml.nvmlDeviceGetHandleByIndex(i)
+            u = pynvml.nvmlDeviceGetUUID(h)
+            u = (u.decode() if isinstance(u, bytes) else u).lower().replace("gpu-", "")
+            if want and want in u:
+                return pynvml, h
+        if not want and pynvml.nvmlDeviceGetCount() == 1:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(0)
+        raise RuntimeError("device not found in NVML")
 
     def start(self):
         try:
+            nv, h = self._nvml_handle()
+        except Exception:
+            nv = None
+        if nv is not None:
+            self.source = "nvml"
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        w = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    except Exception:
+                        break
+                    self.samples.append((time.time(), sm, mx, {n for n, b in bits.items() if rs & b}, w))
+                    time.sleep(self.period_ms / 1000.0)
+            threading.Thread(target=poll, daemon=True).start()
+            return
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 f"-lms", str(self.period_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                text=True)
+                 "-lms", "25"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
+        self.source = "nvidia-smi"
         threading.Thread(target=self._read, daemon=True).start()
 
     def _read(self):
@@ -100,16 +147,17 @@ class ClockSampler:
                 continue
             try:
                 sm, mx = float(parts[1]), float(parts[2])
+                w = float(parts[3])
             except ValueError:
                 continue
-            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-            reasons = {n for n, v in zip(names, parts[5:9]) if v.lower().startswith("active")}
-            self.samples.append((time.time(), sm, mx, reasons))
+            reasons = {n for n, v in zip(self.REASONS, parts[5:9]) if v.lower().startswith("active")}
+            self.samples.append((time.time(), sm, mx, reasons, w))
 
     def mark(self, lo, hi):
         self.t_lo, self.t_hi = lo, hi
 
     def stop(self):
+        self._stop.set()
         if self.proc:
             self.proc.terminate()
             try:
@@ -120,13 +168,15 @@ class ClockSampler:
     def summary(self):
         s = self.samples
         if self.t_lo is not None:
-            inside = [x for x in s if self.t_lo <= x[0] <= self.t_hi]
-            s = inside or s
+            s = [x for x in s if self.t_lo <= x[0] <= self.t_hi]
         if not s:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "source": self.source}
         reasons = sorted(set().union(*[x[3] for x in s]))
-        return {"sm_mhz": statistics.median(x[1] for x in s), "sm_max_mhz": max(x[2] for x in s),
-                "reasons": reasons, "samples": len(s)}
+        return {"sm_mhz": statistics.median(x[1] for x in s), "sm_min_mhz": min(x[1] for x in s),
+                "sm_max_mhz": max(x[2] for x in s), "reasons": reasons, "samples": len(s),
+                "power_w_median": round(statistics.median(x[4] for x in s), 1),
+                "source": self.source}
 
 
 # ---------------------------------------------------------------- distributed
@@ -440,10 +490,24 @@ def make_workload(name, batch=None):
 
 
 # ---------------------------------------------------------------- timing
-def time_steps(fn, steps, warmup, world, stream=None):
+def time_steps(fn, steps, warmup, world, stream=None, min_warm_s=0.0):
+    """Device time of `steps` calls of fn (CUDA events), max over ranks. First
+    `warmup` untimed calls, then (min_warm_s > 0) enough further untimed calls
+    to fill about min_warm_s seconds: a long dense loop settles under the
+    power cap, and timing starts once it has. Every rank runs the same number
+    of calls (the count is the max over ranks)."""
     import torch
+    t_w = time.time()
     for _ in range(warmup):
         fn()
+    if min_warm_s > 0:
+        torch.cuda.synchronize()
+        el = time.time() - t_w
+        per = el / max(1, warmup)
+        extra = int(min(100000, max(0.0, (min_warm_s - el) / max(per, 1e-6))))
+        extra = int(max_over_ranks(float(extra), world))
+        for _ in range(extra):
+            fn()
     barrier(world)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall0 = time.time()
@@ -595,16 +659,17 @@ def measure(w, rank, world, steps, warmup, peaks, peak_kind, sampler=None):
         steps = max(1, steps // reps)
     if sampler:
         sampler.start()
-    ms, (t0, t1) = time_steps(step, steps, warmup, world)
+    ms, (t0, t1) = time_steps(step, steps, warmup, world, min_warm_s=WARM_S)
     if sampler:
         sampler.mark(t0, t1)
     # dominant kernel alone (CUDA events on the launching stream)
-    kms, _ = time_steps(kern, steps, max(1, warmup), world)
+    kms, _ = time_steps(kern, steps, max(1, warmup), world, min_warm_s=WARM_S)
     n = steps * max(1, reps)
     return {"ms_per_step": ms / n, "kernel_ms": kms / n, "graph_reps": reps}
 
 
 def main():
+    global WARM_S
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
@@ -614,10 +679,15 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--warm-s", type=float, default=None,
+                    help="untimed seconds before each timed loop (default %.1f; 0 for "
+                         "profiling runs)" % WARM_S)
     ap.add_argument("--batch", type=int, default=None,
                     help="cfg5 only: sequences per step (default 64; smaller for profiling)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.warm_s is not None:
+        WARM_S = max(0.0, args.warm_s)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -710,7 +780,8 @@ def main():
             "data": "synthetic (seeded N(0,1) inputs of the config's shapes; no dataset)",
             "config": dict(w.describe(world), l2="inputs larger than L2 (no flush)"
                            if is_prefill or isinstance(w, BatchedDecodeWork)
-                           else "rotating caches larger than L2"),
+                           else "rotating caches larger than L2",
+                           untimed_warm_s=WARM_S),
             "cuda_graph_steps": res.get("graph_reps", 0),
             "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": peak_unit,
                          "frac": achieved / peak, "traffic": profile_traffic(tkey) if tkey else None,

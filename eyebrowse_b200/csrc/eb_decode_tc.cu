@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(96)
         if (viss[s]) mbar_drain(bar(kVFull0 + s), (viss[s] - 1) & 1, a.err, kErrTimeoutTma);
       }
     }
+    __syncwarp();  // reconverge before the CTA barrier below
   } else if (warp == 2) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -193,6 +194,7 @@ __global__ void __launch_bounds__(96)
       umma_commit(bar(kFinal));
       mbar_drain(bar(kFinal), 0, a.err, kErrTimeoutMma);
     }
+    __syncwarp();  // reconverge before the CTA barrier below
   } else {
     // ------------------------------------------------------------ rows (warp 0)
     const float* cos_row = a.cos_t ? a.cos_t + (int64_t)pos * (HD / 2) : nullptr;
@@ -444,7 +446,6 @@ __global__ void __launch_bounds__(96)
   tc_fence_before();
   __syncthreads();
   if (warp == 2) {
-    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }

@@ -204,6 +204,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
       for (int s = 0; s < NSTV; s++)
         if (viss[s]) mbar_drain(bar(kVFull0 + s), (viss[s] - 1) & 1, a.err, kErrTimeoutTma);
     }
+    __syncwarp();  // reconverge before the CTA barrier below
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -311,6 +312,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
       umma_commit(bar(kBarFinal));
       mbar_drain(bar(kBarFinal), 0, a.err, kErrTimeoutMma);
     }
+    __syncwarp();  // reconverge before the CTA barrier below
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax rows
     const int t = (warp - 4) >> 2;           // query tile of this warpgroup
@@ -527,7 +529,6 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
-    __syncwarp();  // lane 0 arrives from the MMA loop; dealloc is warp-collective
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
