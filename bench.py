@@ -33,13 +33,16 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from eyebrowse_b200.sharded import gather_heads, head_shard  # noqa: E402
+from eyebrowse_b200.sharded import GatheredOutput, gather_heads, head_shard  # noqa: E402
 
 METRIC = "prefill attn TFLOP/s & decode KV GB/s at 1/2/4/8 B200 vs roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # Untimed seconds before each timed loop: long enough for the SM clock to
 # settle under the 1000 W power cap, so the timed region sees steady clocks.
 WARM_S = 1.5
+# Head-concat exchange for N > 1: "fused" (the attention kernel stores into
+# every rank's output over NVLink) or "nccl" (all-gather + eb_head_concat).
+GATHER = "fused"
 
 
 def load_peaks():
@@ -246,7 +249,10 @@ class PrefillWork:
                 "n_kv_heads": self.Hkv, "head_dim": self.hd, "rope_theta": self.theta,
                 "scale": round(self.scale, 6), "qk_norm": self.qk_norm, "v_norm": self.v_norm,
                 "rope_angles": self.rope_angles or self.hd // 2, "batch": 1,
-                "parallelism": f"heads/{world}" if world > 1 else "1 GPU"}
+                "parallelism": f"heads/{world}" if world > 1 else "1 GPU",
+                "head_concat": ("fused: the attention kernel TMA-stores each output tile "
+                                "into every rank's buffer over NVLink" if GATHER == "fused"
+                                else "NCCL all-gather + eb_head_concat") if world > 1 else None}
 
     def setup(self, rank, world):
         import torch
@@ -282,16 +288,30 @@ class PrefillWork:
         self.layer = eb.make_layer(qw, kw, vw, self.cos, self.sin)
         nb = eb.attention_prefill_workspace_bytes(self.desc, S)
         self.ws = eb.alloc_workspace(nb) if nb else None
-        if world > 1:
+        self.gout = None
+        if world > 1 and GATHER == "fused":
+            # the attention kernel stores every rank's heads into every rank's
+            # `full` over NVLink; two device barriers per step (before, after)
+            self.gout = GatheredOutput(S, self.H, hd, tdt, sh)
+            self.full = self.gout.full
+            self.launches_per_step = 5  # K/V prep, q prep, attention, 2 barriers
+        elif world > 1:
             self.gath = torch.empty(world, S, self.Hl, hd, device="cuda", dtype=tdt)
             self.full = torch.empty(S, self.H, hd, device="cuda", dtype=tdt)
+            self.launches_per_step = 4  # K/V prep, q prep, attention, head concat
         else:
             self.full = self.o
-        self.launches_per_step = 3 + (1 if world > 1 else 0)  # K/V prep, q prep, attention
+            self.launches_per_step = 3  # K/V prep, q prep, attention
         self.bytes_in = sum(t.numel() * t.element_size() for t in (self.q, self.k, self.v))
 
     def step(self):
         eb = self.eb
+        if self.gout is not None:
+            self.gout.barrier()
+            eb.attention_prefill_gather(self.desc, self.layer, self.S, self.q, self.k, self.v,
+                                        self.kc, self.vc, self.gout.gather, self.ws)
+            self.gout.barrier()
+            return
         eb.attention_prefill(self.desc, self.layer, self.S, self.q, self.k, self.v, self.kc,
                              self.vc, self.o, self.ws)
         self._gather()
@@ -302,7 +322,14 @@ class PrefillWork:
                          self.dt)
 
     def kernel_only(self):
-        """The dominant kernel alone: the tensor-core attention (K/V already in the cache)."""
+        """The dominant kernel alone: the tensor-core attention (K/V already in the cache),
+        with its q row-prep launch; with the fused gather, its NVLink stores included.
+        Back-to-back calls store the same values into disjoint head columns, so
+        no barrier is needed between them."""
+        if self.gout is not None:
+            self.eb.attention_prefill_attend_gather(self.desc, self.layer, self.S, self.q,
+                                                    self.kc, self.vc, self.gout.gather, self.ws)
+            return
         self.eb.attention_prefill_attend(self.desc, self.layer, self.S, self.q, self.kc, self.vc,
                                          self.o, self.ws)
 
@@ -669,7 +696,7 @@ def measure(w, rank, world, steps, warmup, peaks, peak_kind, sampler=None):
 
 
 def main():
-    global WARM_S
+    global WARM_S, GATHER
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
@@ -679,6 +706,9 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="N>1 head-concat exchange: fused into the attention kernel "
+                         "(default) or NCCL all-gather + concat")
     ap.add_argument("--warm-s", type=float, default=None,
                     help="untimed seconds before each timed loop (default %.1f; 0 for "
                          "profiling runs)" % WARM_S)
@@ -688,6 +718,7 @@ def main():
     args.warmup = max(3, args.warmup)
     if args.warm_s is not None:
         WARM_S = max(0.0, args.warm_s)
+    GATHER = args.gather
     if args.impl == "reference":
         return run_reference(args)
 

@@ -25,10 +25,18 @@ EXPORTS = (
     "eb_attn_decode", "eb_attn_decode_workspace_bytes", "eb_rope", "eb_kv_write", "eb_rmsnorm",
     "eb_rope_tables", "eb_attention_prefill", "eb_attention_prefill_workspace_bytes",
     "eb_attention_prefill_kv", "eb_attention_prefill_attend",
+    "eb_attention_prefill_gather", "eb_attention_prefill_attend_gather",
     "eb_attention_decode", "eb_attention_decode_batched", "eb_attention_decode_workspace_bytes",
     "eb_workspace_init", "eb_head_concat", "eb_get_device_error",
     "eb_attention_decode_noalloc",
 )
+
+
+class HeadGather(ctypes.Structure):
+    """eb_head_gather: where a head-sharded prefill stores its heads (dst is a
+    host array of device addresses, one per rank)."""
+    _fields_ = [("n_dst", ctypes.c_int32), ("head_offset", ctypes.c_int32),
+                ("n_heads_total", ctypes.c_int64), ("dst", ctypes.POINTER(ctypes.c_uint64))]
 
 
 class EbError(RuntimeError):
@@ -84,6 +92,11 @@ def lib() -> ctypes.CDLL:
     L.eb_attention_prefill.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
     L.eb_attention_prefill_kv.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
     L.eb_attention_prefill_attend.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
+    gp = ctypes.POINTER(HeadGather)
+    L.eb_attention_prefill_gather.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, gp, _vp, _sz,
+                                              _vp]
+    L.eb_attention_prefill_attend_gather.argtypes = [dp, lp, _i64, _vp, _vp, _vp, gp, _vp, _sz,
+                                                     _vp]
     L.eb_attention_prefill_workspace_bytes.restype = _sz
     L.eb_attention_prefill_workspace_bytes.argtypes = [dp, _i64]
     L.eb_attention_decode.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
@@ -222,6 +235,27 @@ def attention_prefill_attend(desc, layer, seq, q, kcache, vcache, o, workspace=N
                                              _ptr(q), _ptr(kcache), _ptr(vcache), _ptr(o),
                                              _ptr(workspace), ws_bytes, _stream(stream)),
            "eb_attention_prefill_attend")
+
+
+def attention_prefill_gather(desc, layer, seq, q, k, v, kcache, vcache, gather: HeadGather,
+                             workspace=None, stream=None):
+    """eb_attention_prefill with the head gather fused into the attention kernel."""
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _check(lib().eb_attention_prefill_gather(ctypes.byref(desc), ctypes.byref(layer), seq,
+                                             _ptr(q), _ptr(k), _ptr(v), _ptr(kcache),
+                                             _ptr(vcache), ctypes.byref(gather), _ptr(workspace),
+                                             ws_bytes, _stream(stream)),
+           "eb_attention_prefill_gather")
+
+
+def attention_prefill_attend_gather(desc, layer, seq, q, kcache, vcache, gather: HeadGather,
+                                    workspace=None, stream=None):
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _check(lib().eb_attention_prefill_attend_gather(ctypes.byref(desc), ctypes.byref(layer), seq,
+                                                    _ptr(q), _ptr(kcache), _ptr(vcache),
+                                                    ctypes.byref(gather), _ptr(workspace),
+                                                    ws_bytes, _stream(stream)),
+           "eb_attention_prefill_attend_gather")
 
 
 def attention_decode_workspace_bytes(desc, batch, max_pos) -> int:

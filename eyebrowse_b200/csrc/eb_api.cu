@@ -313,7 +313,7 @@ int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, in
     a.err = error_word_ptr();
     if (!a.err) return EB_ERR_CUDA;
     return cuda_status(
-        launch_prefill_tc(a, (int)hd, qplanes, nullptr, nullptr, false, workspace, st));
+        launch_prefill_tc(a, (int)hd, qplanes, nullptr, nullptr, false, workspace, nullptr, st));
   }
   SimtArgs sa{};
   sa.q = q;
@@ -470,12 +470,25 @@ int eb_attention_prefill_kv(const eb_attn_desc* d, const eb_attn_layer* L, int64
   return cuda_status(launch_prep_kv(pa, reinterpret_cast<cudaStream_t>(stream)));
 }
 
-int eb_attention_prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq,
-                                const void* q, const void* kcache, const void* vcache, void* o,
-                                void* workspace, size_t workspace_bytes, eb_stream_t stream) {
+static_assert(EB_MAX_GATHER == kMaxGather, "gather destination limit");
+
+// The attention half of a prefill, into o or (g != nullptr) into every
+// rank's gathered buffer.
+static int prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq,
+                          const void* q, const void* kcache, const void* vcache, void* o,
+                          const eb_head_gather* g, void* workspace, size_t workspace_bytes,
+                          eb_stream_t stream) {
   int rc = prefill_check(d, L, seq, workspace, workspace_bytes);
   if (rc != EB_OK || seq == 0) return rc;
-  if (!q || !kcache || !vcache || !o) return EB_ERR_INVALID_ARGUMENT;
+  if (!q || !kcache || !vcache || (!o && !g)) return EB_ERR_INVALID_ARGUMENT;
+  if (g) {
+    if (g->n_dst < 1 || g->n_dst > kMaxGather || g->head_offset < 0 || g->n_heads_total < 1 ||
+        (int64_t)g->head_offset + d->n_heads > g->n_heads_total || !g->dst ||
+        !prefill_tc_supported(d->head_dim))
+      return EB_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < g->n_dst; i++)
+      if (!g->dst[i] || (g->dst[i] & 15)) return EB_ERR_INVALID_ARGUMENT;
+  }
   if (!device_ok()) return EB_ERR_NO_DEVICE;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int hd = d->head_dim;
@@ -512,6 +525,14 @@ int eb_attention_prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, i
     a.o = o;
     a.dtype_o = d->dtype_out;
     a.o_stride = os_of(d);
+    GatherSpec gs{};
+    if (g) {
+      a.o = nullptr;
+      gs.n_dst = g->n_dst;
+      gs.h_off = g->head_offset;
+      gs.n_heads_total = g->n_heads_total;
+      gs.dst = g->dst;
+    }
     a.S = (int)seq;
     a.H = d->n_heads;
     a.Hkv = d->n_kv_heads;
@@ -520,7 +541,7 @@ int eb_attention_prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, i
     if (!a.err) return EB_ERR_CUDA;
     return cuda_status(launch_prefill_tc(a, hd, qprep, kcache, vcache,
                                          d->dtype_cache == EB_BF16, split ? workspace : nullptr,
-                                         st));
+                                         g ? &gs : nullptr, st));
   }
   SimtArgs s{};
   s.q = q;
@@ -544,6 +565,36 @@ int eb_attention_prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, i
   s.scale = d->scale;
   s.batch = 1;
   return cuda_status(launch_attn_simt(s, st));
+}
+
+int eb_attention_prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq,
+                                const void* q, const void* kcache, const void* vcache, void* o,
+                                void* workspace, size_t workspace_bytes, eb_stream_t stream) {
+  return prefill_attend(d, L, seq, q, kcache, vcache, o, nullptr, workspace, workspace_bytes,
+                        stream);
+}
+
+int eb_attention_prefill_attend_gather(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq,
+                                       const void* q, const void* kcache, const void* vcache,
+                                       const eb_head_gather* g, void* workspace,
+                                       size_t workspace_bytes, eb_stream_t stream) {
+  if (!g) return EB_ERR_INVALID_ARGUMENT;
+  return prefill_attend(d, L, seq, q, kcache, vcache, nullptr, g, workspace, workspace_bytes,
+                        stream);
+}
+
+int eb_attention_prefill_gather(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq,
+                                const void* q, const void* k, const void* v, void* kcache,
+                                void* vcache, const eb_head_gather* g, void* workspace,
+                                size_t workspace_bytes, eb_stream_t stream) {
+  int rc = prefill_check(d, L, seq, workspace, workspace_bytes);
+  if (rc != EB_OK || seq == 0) return rc;
+  if (!q || !g) return EB_ERR_INVALID_ARGUMENT;
+  rc = eb_attention_prefill_kv(d, L, seq, k, v, kcache, vcache, workspace, workspace_bytes,
+                               stream);
+  if (rc != EB_OK) return rc;
+  return eb_attention_prefill_attend_gather(d, L, seq, q, kcache, vcache, g, workspace,
+                                            workspace_bytes, stream);
 }
 
 int eb_attention_prefill(const eb_attn_desc* d, const eb_attn_layer* L, int64_t seq,

@@ -121,10 +121,24 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
 struct PrefillArgs {
   void* o;
   int dtype_o;
-  int64_t o_stride;
+  int64_t o_stride;  // elements between output rows
   int S, H, Hkv;
   float scale_log2;
   unsigned* err;
+  // Head gather (n_dst > 0): o is unused; head h of row i goes to row i,
+  // head h_off + h of every destination buffer [S][H_total][hd], stored by
+  // TMA through the destination tensor maps passed beside the arguments.
+  int n_dst;
+  int h_off;
+};
+// Destinations of a head gather: up to kMaxGather buffers [S][H_total][hd]
+// in the output dtype (this GPU's and its peers', mapped here).
+constexpr int kMaxGather = 8;
+struct GatherSpec {
+  int n_dst;
+  int h_off;
+  int64_t n_heads_total;
+  const uint64_t* dst;  // host array of n_dst device addresses
 };
 // q16: the prepared query rows [S][H][hd] in the MMA operand type (RMSNorm +
 // RoPE already applied by launch_prep_kv), or their f16 hi/lo planes when
@@ -132,7 +146,8 @@ struct PrefillArgs {
 // f16/bf16). split: f16 hi/lo K/V planes when the cache is f32 (k16/v16
 // unused then).
 cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* q16, const void* k16,
-                              const void* v16, bool bf16, const void* split, cudaStream_t st);
+                              const void* v16, bool bf16, const void* split,
+                              const GatherSpec* gather, cudaStream_t st);
 bool prefill_tc_supported(int hd);
 
 }  // namespace eb

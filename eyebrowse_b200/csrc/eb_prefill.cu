@@ -29,6 +29,7 @@
 // keeps ~21 mantissa bits on f16 tensor cores).
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "eb_common.cuh"
@@ -73,10 +74,33 @@ struct PfCfg {
   static_assert(BN % 32 == 0 && BN <= 128, "kv tile");
   static_assert(TMEM_COLS <= 512, "tensor memory budget");
   static_assert(SMEM <= 232448, "shared memory budget");
+  // Head-gather epilogue: tile t's O stages at [t*STG, (t+1)*STG) from the
+  // start of shared memory (q and the K/V rings are idle by then), as
+  // 128-byte-swizzled boxes of [128 rows x 128 B].
+  static constexpr int STG = 128 * HD * 4;  // room for f32 output
+  static_assert(NQ * STG <= BAR_OFF, "gather staging area");
 };
 
 // Barrier slots.
 enum { kBarQ = 0, kBarFinal = 1, kBarS0 = 2 };
+
+// Tensor maps of the head-gather destinations (see GatherSpec).
+struct GatherMaps {
+  CUtensorMap m[kMaxGather];
+};
+
+// Named barrier over n threads that also ANDs a predicate across them, so
+// every participant takes the same branch afterwards.
+__device__ __forceinline__ bool named_bar_and(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
 
 
 
@@ -87,7 +111,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
                       const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV,
                       const __grid_constant__ CUtensorMap tmKlo,
-                      const __grid_constant__ CUtensorMap tmVlo, PrefillArgs a) {
+                      const __grid_constant__ CUtensorMap tmVlo,
+                      const __grid_constant__ GatherMaps gmaps, PrefillArgs a) {
   using C = PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>;
   constexpr int NSB = C::NSB;
   extern __shared__ uint8_t smem_raw[];
@@ -489,39 +514,78 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     // is outstanding, and with two S buffers PV(n-2) can still be in flight.
     bool got_f = ok && mbar_wait(bar(kBarFinal), 0, abort_flag, a.err, kErrTimeoutEpilogue);
     __syncwarp();
-    if (__all_sync(0xffffffffu, got_f)) {
+    const bool warp_ok = __all_sync(0xffffffffu, got_f);
+    const int esz = a.dtype_o == kF32 ? 4 : 2;
+    const uint32_t stg = sQ + t * C::STG;
+    if (warp_ok) {
       tc_fence_after();
       const float inv_l = 1.f / l_run;
       const int64_t obase = (int64_t)q_row * a.o_stride + (int64_t)h * HD;
 #pragma unroll 1
       for (int c = 0; c < HD / 32; c++) {
         uint32_t o[32];
+        __syncwarp();  // rows past S skip the stores: reconverge for the warp-wide load
         tmem_ld32(tO + c * 32, o);
         tmem_ld_wait();
-        if (valid) {
-          if (a.dtype_o == kF32) {
-            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.o) + obase + c * 32);
+        if (!valid && a.n_dst == 0) continue;
+        // this row's 32 columns as 16-byte words: 8 for f32, 4 for f16/bf16
+        uint4 wv[8];
+        if (a.dtype_o == kF32) {
 #pragma unroll
-            for (int i = 0; i < 8; i++)
-              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l,
-                                   __uint_as_float(o[4 * i + 1]) * inv_l,
-                                   __uint_as_float(o[4 * i + 2]) * inv_l,
-                                   __uint_as_float(o[4 * i + 3]) * inv_l);
-          } else {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.o) + obase + c * 32);
+          for (int i = 0; i < 8; i++)
+            wv[i] = make_uint4(__float_as_uint(__uint_as_float(o[4 * i]) * inv_l),
+                               __float_as_uint(__uint_as_float(o[4 * i + 1]) * inv_l),
+                               __float_as_uint(__uint_as_float(o[4 * i + 2]) * inv_l),
+                               __float_as_uint(__uint_as_float(o[4 * i + 3]) * inv_l));
+        } else {
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-              uint32_t w[4];
+          for (int i = 0; i < 4; i++) {
+            uint32_t w[4];
 #pragma unroll
-              for (int k = 0; k < 4; k++) {
-                const float lo = __uint_as_float(o[8 * i + 2 * k]) * inv_l;
-                const float hi = __uint_as_float(o[8 * i + 2 * k + 1]) * inv_l;
-                w[k] = a.dtype_o == kBF16 ? pack_bf162(lo, hi) : pack_half2(lo, hi);
-              }
-              dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int k = 0; k < 4; k++) {
+              const float lo = __uint_as_float(o[8 * i + 2 * k]) * inv_l;
+              const float hi = __uint_as_float(o[8 * i + 2 * k + 1]) * inv_l;
+              w[k] = a.dtype_o == kBF16 ? pack_bf162(lo, hi) : pack_half2(lo, hi);
             }
+            wv[i] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
+        const int nw = a.dtype_o == kF32 ? 8 : 4;
+        if (a.n_dst == 0) {
+          uint4* d = reinterpret_cast<uint4*>(static_cast<char*>(a.o) + (obase + c * 32) * esz);
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            if (i < nw) d[i] = wv[i];
+        } else {
+          // staging: 16-byte chunk j of the row's bytes sits in box j / 8
+          const int j0 = c * 32 * esz / 16;
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            if (i >= nw) break;
+            const int j = j0 + i;
+            const uint32_t sa = stg + (j >> 3) * C::TILE128 + sw128_offset(r, j & 7);
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sa), "r"(wv[i].x),
+                         "r"(wv[i].y), "r"(wv[i].z), "r"(wv[i].w)
+                         : "memory");
+          }
+        }
+      }
+    }
+    if (a.n_dst > 0) {
+      // The tile's 128 threads have staged it (every warp arrives here, and
+      // the stores go out only if all of them completed); one thread stores
+      // it to every destination by TMA and waits only until shared memory has
+      // been read: the writes over NVLink drain while the next CTA starts.
+      // Rows past S fall outside the maps and are not written.
+      fence_async_smem();
+      const bool tile_ok = named_bar_and(1 + t, 128, warp_ok);
+      if (tile_ok && r == 0) {
+        const int nbox = HD * esz / 128;
+        for (int d = 0; d < a.n_dst; d++)
+          for (int bx = 0; bx < nbox; bx++)
+            tma_store_3d(&gmaps.m[d], stg + bx * C::TILE128, bx * (128 / esz), a.h_off + h, q0);
+        tma_store_commit();
+        tma_store_wait_read();
       }
     }
   }
@@ -565,9 +629,29 @@ bool make_kv_map(CUtensorMap* m, const void* base, int S, int Hkv, int hd, int B
   return r == CUDA_SUCCESS;
 }
 
+// 3-D map over a gathered output [S][H_total][hd] of dtype dt (16-bit or
+// f32), box {128 bytes of one head row, 1 head, 128 rows}, 128-byte swizzle.
+static bool make_out_map(CUtensorMap* m, uint64_t base, int S, int64_t h_total, int hd, int dt) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const int es = dt == kF32 ? 4 : 2;
+  cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)h_total, (cuuint64_t)S};
+  cuuint64_t strides[2] = {(cuuint64_t)hd * es, (cuuint64_t)(h_total * hd * es)};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / es), 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType ty = dt == kF32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dt == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(m, ty, 3, reinterpret_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV>
 static cudaError_t run_prefill(const PrefillArgs& a, const void* q16, const void* k16,
-                               const void* v16, const void* split, cudaStream_t st) {
+                               const void* v16, const void* split, const GatherSpec* g,
+                               cudaStream_t st) {
   using C = PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>;
   auto kern = prefill_tc_kernel<HD, BN, NQ, SPLIT, BF16, NSTK, NSTV>;
   static unsigned configured = 0;  // one bit per device
@@ -604,43 +688,57 @@ static cudaError_t run_prefill(const PrefillArgs& a, const void* q16, const void
     mkl = mk;
     mvl = mv;
   }
+  GatherMaps gm;
+  memset(&gm, 0, sizeof(gm));
+  PrefillArgs ka = a;
+  ka.n_dst = 0;
+  if (g && g->n_dst > 0) {
+    if (g->n_dst > kMaxGather) return cudaErrorInvalidValue;
+    for (int d = 0; d < g->n_dst; d++)
+      if (!make_out_map(&gm.m[d], g->dst[d], a.S, g->n_heads_total, HD, a.dtype_o))
+        return cudaErrorInvalidValue;
+    ka.n_dst = g->n_dst;
+    ka.h_off = g->h_off;
+  }
   const int n_qt = (a.S + 127) / 128;
-  kern<<<(unsigned)(n_qt * (a.H / NQ)), C::THREADS, C::SMEM, st>>>(mq, mql, mk, mv, mkl, mvl, a);
+  kern<<<(unsigned)(n_qt * (a.H / NQ)), C::THREADS, C::SMEM, st>>>(mq, mql, mk, mv, mkl, mvl, gm,
+                                                                     ka);
   return cudaGetLastError();
 }
 
 bool prefill_tc_supported(int hd) { return hd == 64 || hd == 128 || hd == 256; }
 
 cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* q16, const void* k16,
-                              const void* v16, bool bf16, const void* split, cudaStream_t st) {
+                              const void* v16, bool bf16, const void* split,
+                              const GatherSpec* g, cudaStream_t st) {
   // Two query tiles per CTA when the heads of a GQA group pair up.
   const bool pair = ((a.H / a.Hkv) % 2) == 0;
   if (split) {
     switch (hd) {
       case 64:
-        return run_prefill<64, 128, 1, true, false, 2, 2>(a, q16, k16, v16, split, st);
-      case 128: return run_prefill<128, 64, 1, true, false, 2, 2>(a, q16, k16, v16, split, st);
-      case 256: return run_prefill<256, 32, 1, true, false, 1, 1>(a, q16, k16, v16, split, st);
+        return run_prefill<64, 128, 1, true, false, 2, 2>(a, q16, k16, v16, split, g, st);
+      case 128: return run_prefill<128, 64, 1, true, false, 2, 2>(a, q16, k16, v16, split, g, st);
+      case 256: return run_prefill<256, 32, 1, true, false, 1, 1>(a, q16, k16, v16, split, g, st);
     }
   } else if (bf16) {
     switch (hd) {
       case 64:
-        return pair ? run_prefill<64, 128, 2, false, true, 4, 3>(a, q16, k16, v16, split, st)
-                    : run_prefill<64, 128, 1, false, true, 4, 3>(a, q16, k16, v16, split, st);
+        return pair ? run_prefill<64, 128, 2, false, true, 4, 3>(a, q16, k16, v16, split, g, st)
+                    : run_prefill<64, 128, 1, false, true, 4, 3>(a, q16, k16, v16, split, g, st);
       case 128:
-        return pair ? run_prefill<128, 128, 2, false, true, 3, 2>(a, q16, k16, v16, split, st)
-                    : run_prefill<128, 128, 1, false, true, 3, 2>(a, q16, k16, v16, split, st);
-      case 256: return run_prefill<256, 64, 1, false, true, 2, 2>(a, q16, k16, v16, split, st);
+        return pair ? run_prefill<128, 128, 2, false, true, 3, 2>(a, q16, k16, v16, split, g, st)
+                    : run_prefill<128, 128, 1, false, true, 3, 2>(a, q16, k16, v16, split, g, st);
+      case 256: return run_prefill<256, 64, 1, false, true, 2, 2>(a, q16, k16, v16, split, g, st);
     }
   } else {
     switch (hd) {
       case 64:
-        return pair ? run_prefill<64, 128, 2, false, false, 4, 3>(a, q16, k16, v16, split, st)
-                    : run_prefill<64, 128, 1, false, false, 4, 3>(a, q16, k16, v16, split, st);
+        return pair ? run_prefill<64, 128, 2, false, false, 4, 3>(a, q16, k16, v16, split, g, st)
+                    : run_prefill<64, 128, 1, false, false, 4, 3>(a, q16, k16, v16, split, g, st);
       case 128:
-        return pair ? run_prefill<128, 128, 2, false, false, 3, 2>(a, q16, k16, v16, split, st)
-                    : run_prefill<128, 128, 1, false, false, 3, 2>(a, q16, k16, v16, split, st);
-      case 256: return run_prefill<256, 64, 1, false, false, 2, 2>(a, q16, k16, v16, split, st);
+        return pair ? run_prefill<128, 128, 2, false, false, 3, 2>(a, q16, k16, v16, split, g, st)
+                    : run_prefill<128, 128, 1, false, false, 3, 2>(a, q16, k16, v16, split, g, st);
+      case 256: return run_prefill<256, 64, 1, false, false, 2, 2>(a, q16, k16, v16, split, g, st);
     }
   }
   return cudaErrorNotSupported;

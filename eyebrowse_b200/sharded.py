@@ -1,11 +1,17 @@
 """Head-sharded attention across GPUs: one process per GPU, torch.distributed
-(NCCL) for the single exchange at the head-concat boundary.
+for the plumbing, and a single exchange at the head-concat boundary.
 
 Attention is independent per KV-head group, so rank g of G owns KV heads
 [g*Hkv/G, (g+1)*Hkv/G) and their query heads, keeps its own cache slice
 [max_seq, Hkv/G, hd] and runs the fused call on its slice with no traffic to
-other ranks. The per-rank outputs [rows, H/G, hd] are all-gathered into
-[G, rows, H/G, hd] and eb_head_concat restores [rows, H, hd].
+other ranks. The per-rank outputs [rows, H/G, hd] meet at the head-concat
+boundary in one of two ways:
+  - GatheredOutput + eb_attention_prefill_gather: the attention kernel stores
+    every finished output tile straight into every rank's [rows, H, hd]
+    buffer over NVLink (TMA stores into peer memory) while the rest of the
+    kernel runs; no separate collective runs.
+  - gather_heads: NCCL all-gather into [G, rows, H/G, hd], then
+    eb_head_concat restores [rows, H, hd] (the library-collective baseline).
 """
 from __future__ import annotations
 
@@ -56,6 +62,39 @@ def gather_heads(o_local, gath, full, world: int, rows: int, heads_per: int, hea
     import eyebrowse_b200 as eb
     dist.all_gather_into_tensor(gath, o_local, group=group)
     eb.head_concat(gath, full, world, rows, heads_per, head_dim, dtype_code)
+
+
+class GatheredOutput:
+    """The gathered [rows, n_heads, head_dim] output of a head-sharded prefill,
+    held in torch symmetric memory (mapped into every rank's address space)
+    so that eb_attention_prefill_gather can store each rank's heads into every
+    rank's copy. `gather` is the eb_head_gather for this rank's shard.
+
+    Use: barrier(); eyebrowse_b200.attention_prefill_gather(..., gather);
+    barrier(). The first barrier keeps a rank from writing into a buffer a
+    peer is still reading; the second makes every rank's stores visible
+    before anyone reads `full`."""
+
+    def __init__(self, rows: int, n_heads: int, head_dim: int, dtype, shard: HeadShard,
+                 group=None):
+        import ctypes
+
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        import eyebrowse_b200 as eb
+        grp = group or dist.group.WORLD
+        self.full = symm_mem.empty(rows, n_heads, head_dim, dtype=dtype, device="cuda")
+        self.handle = symm_mem.rendezvous(self.full, grp.group_name)
+        world, rank = self.handle.world_size, self.handle.rank
+        off = self.full.data_ptr() - self.handle.buffer_ptrs[rank]
+        self._dst = (ctypes.c_uint64 * world)(*[p + off for p in self.handle.buffer_ptrs])
+        self.gather = eb.HeadGather(n_dst=world, head_offset=shard.h0, n_heads_total=n_heads,
+                                    dst=ctypes.cast(self._dst, ctypes.POINTER(ctypes.c_uint64)))
+
+    def barrier(self):
+        """Device-side barrier across the group's GPUs on the current stream."""
+        self.handle.barrier(channel=0)
 
 
 def concat_heads_host(shards):

@@ -161,6 +161,41 @@ EB_API int eb_attention_prefill_attend(const eb_attn_desc* desc, const eb_attn_l
                                        const void* vcache, void* o, void* workspace,
                                        size_t workspace_bytes, eb_stream_t stream);
 
+/* Head-sharded prefill with the gather fused into the attention kernel: the
+ * kernel of the rank that owns heads [head_offset, head_offset + n_heads)
+ * stores each finished output tile straight into the gathered [seq,
+ * n_heads_total, head_dim] buffer of every rank (TMA stores over NVLink, at
+ * most EB_MAX_GATHER buffers), so no all-gather + eb_head_concat follows. The
+ * tiles leave as they finish, while the rest of the kernel runs.
+ *   dst: HOST array of n_dst device addresses, each rank's gathered buffer
+ *        in desc->dtype_out as mapped in this process (peer memory),
+ *        16-byte aligned.
+ * Nothing else may write those buffers during the call. The caller orders
+ * this call after every rank's last read of its buffer, and every rank's
+ * reads after every rank's call (a cross-GPU barrier before and after).
+ * Head dims other than 64/128/256 are not supported here
+ * (EB_ERR_INVALID_ARGUMENT). No reference counterpart: it is the multi-GPU
+ * split by KV-head group. */
+#define EB_MAX_GATHER 8
+typedef struct eb_head_gather {
+  int32_t n_dst;
+  int32_t head_offset;
+  int64_t n_heads_total;
+  const uint64_t* dst;
+} eb_head_gather;
+
+EB_API int eb_attention_prefill_gather(const eb_attn_desc* desc, const eb_attn_layer* layer,
+                                       int64_t seq, const void* q, const void* k, const void* v,
+                                       void* kcache, void* vcache, const eb_head_gather* gather,
+                                       void* workspace, size_t workspace_bytes,
+                                       eb_stream_t stream);
+EB_API int eb_attention_prefill_attend_gather(const eb_attn_desc* desc,
+                                              const eb_attn_layer* layer, int64_t seq,
+                                              const void* q, const void* kcache,
+                                              const void* vcache, const eb_head_gather* gather,
+                                              void* workspace, size_t workspace_bytes,
+                                              eb_stream_t stream);
+
 /* One decode step at position pos (Attention::decode,
  * crates/eyebrowse-nn/src/attention.rs:120-185): q [n_heads, head_dim],
  * k/v [n_kv_heads, head_dim] are the projection outputs of the new token; the

@@ -1,13 +1,17 @@
-"""Multi-GPU parity of the head-sharded prefill and batched decode (NCCL).
+"""Multi-GPU parity of the head-sharded prefill and batched decode.
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N \
         --master-addr 127.0.0.1 --master-port P tests/mgpu_parity.py
 
 Every rank builds the same seeded full inputs, runs its KV-head group
 through the C ABI, and the outputs are all-gathered and head-concatenated
-on every rank (eyebrowse_b200.sharded.gather_heads). Rank 0 checks the full
-result against the oracle at max-abs <= 2e-3, rel-L2 <= 1e-3 and exits
-non-zero on a mismatch. Not collected by pytest: it needs N processes.
+on every rank over NCCL (eyebrowse_b200.sharded.gather_heads). Rank 0 checks
+the full result against the oracle at max-abs <= 2e-3, rel-L2 <= 1e-3. The
+prefill then runs again with the gather fused into the attention kernel
+(eb_attention_prefill_gather: TMA stores into every rank's symmetric-memory
+buffer), and every rank checks that its gathered copy equals the NCCL
+result bit for bit. Exits non-zero on
+any mismatch. Not collected by pytest: it needs N processes.
 """
 import datetime
 import os
@@ -24,7 +28,7 @@ def main() -> int:
     import torch.distributed as dist
 
     import eyebrowse_b200 as eb
-    from eyebrowse_b200.sharded import gather_heads, head_shard
+    from eyebrowse_b200.sharded import GatheredOutput, gather_heads, head_shard
     from oracle import oracle as orc
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -65,6 +69,22 @@ def main() -> int:
         print(f"[mgpu] world={world} prefill rows [{S-96},{S}) x {H} heads: max_abs={ma:.2e} "
               f"rel_l2={rl:.2e}", flush=True)
         ok &= ma <= 2e-3 and rl <= 1e-3
+    # ---- the same prefill with the head gather fused into the kernel
+    g = GatheredOutput(S, H, hd, f16, sh)
+    g.full.fill_(float("nan"))
+    g.barrier()
+    for _ in range(2):  # twice: the second call overwrites the first
+        g.barrier()
+        eb.attention_prefill_gather(desc, layer, S, dev(q[:, sh.h0:sh.h1]),
+                                    dev(k[:, sh.kv0:sh.kv1]), dev(v[:, sh.kv0:sh.kv1]), kc, vc,
+                                    g.gather, ws)
+        g.barrier()
+    torch.cuda.synchronize()
+    same = torch.equal(g.full, full)
+    print(f"[mgpu] rank {rank} fused gather (TMA stores over NVLink) == NCCL gather: {same}",
+          flush=True)
+    ok &= same
+    del g
     # ---- batched decode: config-5 geometry, 8 sequences, f16 caches
     B, max_seq = 8, 4096
     pos = (np.random.default_rng(12).integers(512, max_seq, size=B) - 1).astype(np.int32)
