@@ -75,7 +75,10 @@ __global__ void __launch_bounds__(96)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::BAR_OFF + 384);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::BAR_OFF + 392);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  constexpr int kQ = 0, kFinal = 1, kSFull0 = 2, kPFull = 4, kODone = 5, kKFull0 = 6;
+  // one S-full and one P-full barrier per S buffer: with two buffers the
+  // softmax may finish P(j+1) before the MMA thread's wait sees P(j), and a
+  // single P barrier would then be two phases ahead of that parity wait
+  constexpr int kQ = 0, kFinal = 1, kSFull0 = 2, kPFull0 = 4, kODone = 6, kKFull0 = 7;
   constexpr int kKEmpty0 = kKFull0 + NST, kVFull0 = kKEmpty0 + NST, kVEmpty0 = kVFull0 + NST;
   constexpr int kNumBars = kVEmpty0 + NST;
   static_assert(kNumBars * 8 <= 384, "barrier area");
@@ -86,7 +89,8 @@ __global__ void __launch_bounds__(96)
     mbar_init(bar(kFinal), 1);
     mbar_init(bar(kSFull0), 1);
     mbar_init(bar(kSFull0 + 1), 1);
-    mbar_init(bar(kPFull), 32);
+    mbar_init(bar(kPFull0), 32);
+    mbar_init(bar(kPFull0 + 1), 32);
     for (int i = kODone; i < kNumBars; i++) mbar_init(bar(i), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(96)
           umma_commit(bar(kSFull0 + (nj & 1)));
           umma_commit(bar(kKEmpty0 + nst));
         }
-        if (!mbar_wait(bar(kPFull), j & 1, abort_flag, a.err, kErrTimeoutMma) ||
+        if (!mbar_wait(bar(kPFull0 + (j & 1)), (j >> 1) & 1, abort_flag, a.err, kErrTimeoutMma) ||
             !mbar_wait(bar(kVFull0 + st), (j / NST) & 1, abort_flag, a.err, kErrTimeoutMma))
           break;
         tc_fence_after();
@@ -376,7 +380,7 @@ __global__ void __launch_bounds__(96)
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(bar(kPFull));
+      mbar_arrive(bar(kPFull0 + buf));
     }
     // ---- partial or final output
     bool got_f = ok && mbar_wait(bar(kFinal), 0, abort_flag, a.err, kErrTimeoutEpilogue);

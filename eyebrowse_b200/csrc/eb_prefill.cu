@@ -60,7 +60,7 @@ struct PfCfg {
   static constexpr int V_OFF = Q_BYTES + NSTK * K_BYTES;  // V ring follows the K ring
   static constexpr int BAR_OFF = V_OFF + NSTV * K_BYTES;
   static constexpr int SMEM = BAR_OFF + 512 + 1024;  // barriers/flags + alignment slack
-  static constexpr int NSB = NQ == 1 ? 2 : 1;
+  static constexpr int NSB = (NQ == 1 || NQ * HD + NQ * 2 * BN <= 512) ? 2 : 1;
   // TMEM columns: the O accumulators first ([t*HD, (t+1)*HD)), then the S/P
   // buffers; every MMA destination starts at a column aligned to its width.
   static constexpr int S_COL0 = NQ * HD;
@@ -126,8 +126,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   // barrier index map
   constexpr int kSFull0 = kBarS0;                 // [NQ][NSB]
-  constexpr int kPFull0 = kSFull0 + NQ * NSB;     // [NQ]
-  constexpr int kODone0 = kPFull0 + NQ;           // [NQ]
+  constexpr int kPFull0 = kSFull0 + NQ * NSB;     // [NQ][NSB]
+  constexpr int kODone0 = kPFull0 + NQ * NSB;     // [NQ]
   constexpr int kKFull0 = kODone0 + NQ;           // [NSTK]
   constexpr int kKEmpty0 = kKFull0 + NSTK;        // [NSTK]
   constexpr int kVFull0 = kKEmpty0 + NSTK;        // [NSTV]
@@ -295,17 +295,26 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         const int sv = j % NSTV;
         const int nj = j + 1, nsk = nj % NSTK;
         if (NSB == 2 && nj < n_tiles) {
-          // single query tile: S(j+1) goes to the other buffer ahead of PV(j)
+          // S_t(j+1) goes to the other buffer ahead of PV_t(j), so it is ready
+          // when the softmax of j finishes. That buffer's P_t(j-1) was read by
+          // PV_t(j-1), issued before and executed in order.
           if (!mbar_wait(bar(kKFull0 + nsk), (nj / NSTK) & 1, abort_flag, a.err, kErrTimeoutMma))
             break;
           tc_fence_after();
-          issue_qk(0, nj & 1, nsk);
-          umma_commit(bar(kSFull0 + (nj & 1)));
+#pragma unroll
+          for (int t = 0; t < NQ; t++) {
+            issue_qk(t, nj & 1, nsk);
+            umma_commit(bar(kSFull0 + t * NSB + (nj & 1)));
+          }
           umma_commit(bar(kKEmpty0 + nsk));
         }
 #pragma unroll
         for (int t = 0; t < NQ; t++) {
-          if (!mbar_wait(bar(kPFull0 + t), j & 1, abort_flag, a.err, kErrTimeoutMma)) {
+          // One P barrier per S buffer: with two buffers the softmax may finish
+          // P(j+1) before this wait sees P(j), and a per-tile barrier would
+          // then be two phases ahead of its parity wait.
+          if (!mbar_wait(bar(kPFull0 + t * NSB + j % NSB), (j / NSB) & 1, abort_flag, a.err,
+                         kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -363,7 +372,10 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
       tc_fence_after();
       const int k0 = j * BN;
       const bool diag = k0 + BN - 1 > q_row;  // tile crosses the causal diagonal
-      // pass 1: the row max (the S row is the only live data here)
+      // pass 1: the row max (the S row is the only live data here). A row of
+      // at most 64 columns stays in registers for pass 2 (no second load).
+      constexpr bool KEEP = BN <= 64;
+      float xk[KEEP ? BN : 1];
       float mt;
       {
         float x[BN];
@@ -390,6 +402,10 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
 #pragma unroll
           for (int i = 0; i < 8; i++) mc[i] = fmax3(mc[i], x[c + i], x[c + 8 + i]);
         mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[5]), fmaxf(mc[6], mc[7]));
+        if constexpr (KEEP) {
+#pragma unroll
+          for (int c = 0; c < BN; c++) xk[c] = x[c];
+        }
       }
       const float ms = mt * sl2;
       // lazy rescale: warp-uniform, since tcgen05.ld/st of O are warp-collective
@@ -422,9 +438,9 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         l_run *= corr;
         m_run = m_new;
       }
-      // pass 2: re-read S in halves, P = exp2(s*scale - m) -> 16-bit operand in
-      // TMEM over the columns already consumed (P half h lands in S columns
-      // [h*HALF/2, (h+1)*HALF/2), which this pass has read before)
+      // pass 2: S in halves (re-read from TMEM unless kept), P = exp2(s*scale
+      // - m) -> 16-bit operand in TMEM over the columns already consumed (P
+      // half h lands in S columns [h*HALF/2, (h+1)*HALF/2), read before)
       const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m_run, -m_run);
       uint64_t rsum2[4];
 #pragma unroll
@@ -433,19 +449,24 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
 #pragma unroll
       for (int hbase = 0; hbase < BN; hbase += HALF) {
         float x[HALF];
-        {
-          uint32_t u[HALF];
+        if constexpr (KEEP) {  // HALF == BN: the whole (masked) row from pass 1
 #pragma unroll
-          for (int c = 0; c < HALF / 32; c++)
-            tmem_ld32(tS + hbase + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
-          tmem_ld_wait();
+          for (int c = 0; c < HALF; c++) x[c] = xk[c];
+        } else {
+          {
+            uint32_t u[HALF];
 #pragma unroll
-          for (int c = 0; c < HALF; c++) x[c] = __uint_as_float(u[c]);
-        }
-        if (diag) {
+            for (int c = 0; c < HALF / 32; c++)
+              tmem_ld32(tS + hbase + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
+            tmem_ld_wait();
 #pragma unroll
-          for (int c = 0; c < HALF; c++)
-            if (k0 + hbase + c > q_row) x[c] = -INFINITY;
+            for (int c = 0; c < HALF; c++) x[c] = __uint_as_float(u[c]);
+          }
+          if (diag) {
+#pragma unroll
+            for (int c = 0; c < HALF; c++)
+              if (k0 + hbase + c > q_row) x[c] = -INFINITY;
+          }
         }
         uint32_t ph[HALF / 2];
         uint32_t pl[SPLIT ? HALF / 2 : 1];
@@ -506,7 +527,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(bar(kPFull0 + t));
+      mbar_arrive(bar(kPFull0 + t * NSB + b));
     }
     // ---- epilogue: O / l -> global
     // Wait on the barrier the MMA thread commits once, after its last MMA: a
