@@ -372,10 +372,11 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
       tc_fence_after();
       const int k0 = j * BN;
       const bool diag = k0 + BN - 1 > q_row;  // tile crosses the causal diagonal
-      // pass 1: the row max (the S row is the only live data here). A row of
-      // at most 64 columns stays in registers for pass 2 (no second load).
-      constexpr bool KEEP = BN <= 64;
-      float xk[KEEP ? BN : 1];
+      // pass 1: the row max (the S row is the only live data here). The first
+      // (up to) 64 columns stay in registers for pass 2, which re-reads only
+      // the rest from TMEM.
+      constexpr int KEEP = BN < 64 ? BN : 64;
+      float xk[KEEP];
       float mt;
       {
         float x[BN];
@@ -402,10 +403,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
 #pragma unroll
           for (int i = 0; i < 8; i++) mc[i] = fmax3(mc[i], x[c + i], x[c + 8 + i]);
         mt = fmax3(fmax3(mc[0], mc[1], mc[2]), fmax3(mc[3], mc[4], mc[5]), fmaxf(mc[6], mc[7]));
-        if constexpr (KEEP) {
 #pragma unroll
-          for (int c = 0; c < BN; c++) xk[c] = x[c];
-        }
+        for (int c = 0; c < KEEP; c++) xk[c] = x[c];
       }
       const float ms = mt * sl2;
       // lazy rescale: warp-uniform, since tcgen05.ld/st of O are warp-collective
@@ -449,7 +448,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
 #pragma unroll
       for (int hbase = 0; hbase < BN; hbase += HALF) {
         float x[HALF];
-        if constexpr (KEEP) {  // HALF == BN: the whole (masked) row from pass 1
+        if (hbase == 0) {  // HALF == KEEP: the first (masked) columns from pass 1
 #pragma unroll
           for (int c = 0; c < HALF; c++) x[c] = xk[c];
         } else {
