@@ -127,7 +127,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
   // barrier index map
   constexpr int kSFull0 = kBarS0;                 // [NQ][NSB]
   constexpr int kPFull0 = kSFull0 + NQ * NSB;     // [NQ][NSB]
-  constexpr int kODone0 = kPFull0 + NQ * NSB;     // [NQ]
+  constexpr int kP0Full0 = kPFull0 + NQ * NSB;    // [NQ][NSB]: first half of P (BN = 128)
+  constexpr int kODone0 = kP0Full0 + NQ * NSB;    // [NQ]
   constexpr int kKFull0 = kODone0 + NQ;           // [NSTK]
   constexpr int kKEmpty0 = kKFull0 + NSTK;        // [NSTK]
   constexpr int kVFull0 = kKEmpty0 + NSTK;        // [NSTV]
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     mbar_init(bar(kBarQ), 1);
     mbar_init(bar(kBarFinal), 1);
     for (int i = kSFull0; i < kPFull0; i++) mbar_init(bar(i), 1);
-    for (int i = kPFull0; i < kODone0; i++) mbar_init(bar(i), 128);
+    for (int i = kPFull0; i < kODone0; i++) mbar_init(bar(i), 128);  // P and P-half-0
     for (int i = kODone0; i < kNumBars; i++) mbar_init(bar(i), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -256,7 +257,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         }
       };
       // O_t += P_t V, P_t read from tensor memory (the S buffer it replaced)
-      auto issue_pv = [&](int t, int b, int sv, bool first) {
+      // keys [16*kk0, 16*kk1) of the tile
+      auto issue_pv = [&](int t, int b, int sv, bool first, int kk0, int kk1) {
         const uint32_t vst = sV + sv * C::K_BYTES;
         const uint32_t tP = tmem + C::S_COL0 + (t * NSB + b) * BN;
         const uint32_t tO = tmem + t * HD;
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
           const int pa = (pass == 2) ? 1 : 0;  // Ph Vh, Ph Vl, Pl Vh
           const int vb = (pass == 1) ? 1 : 0;
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; kk++) {
+          for (int kk = kk0; kk < kk1; kk++) {
             const uint64_t bd =
                 sdesc_sw128(vst + vb * C::HB * C::KV_BOX + kk * 16 * 128, C::KV_BOX, 1024);
             // column of P elements [16kk, 16kk+16) in the softmax's layout
@@ -312,9 +314,10 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         for (int t = 0; t < NQ; t++) {
           // One P barrier per S buffer: with two buffers the softmax may finish
           // P(j+1) before this wait sees P(j), and a per-tile barrier would
-          // then be two phases ahead of its parity wait.
-          if (!mbar_wait(bar(kPFull0 + t * NSB + j % NSB), (j / NSB) & 1, abort_flag, a.err,
-                         kErrTimeoutMma)) {
+          // then be two phases ahead of its parity wait. With BN = 128 this
+          // first waits for P's first half only.
+          if (!mbar_wait(bar((BN == 128 ? kP0Full0 : kPFull0) + t * NSB + j % NSB), (j / NSB) & 1,
+                         abort_flag, a.err, kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -324,7 +327,20 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
             break;
           }
           tc_fence_after();
-          issue_pv(t, j % NSB, sv, j == 0);
+          if constexpr (BN == 128) {
+            // P arrives in two halves: PV over keys [0, 64) runs while the
+            // softmax still computes the rest
+            issue_pv(t, j % NSB, sv, j == 0, 0, BN / 32);
+            if (!mbar_wait(bar(kPFull0 + t * NSB + j % NSB), (j / NSB) & 1, abort_flag, a.err,
+                           kErrTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, j % NSB, sv, false, BN / 32, BN / 16);
+          } else {
+            issue_pv(t, j % NSB, sv, j == 0, 0, BN / 16);
+          }
           umma_commit(bar(kODone0 + t));
           if (NSB == 1 && nj < n_tiles) {
             // S_t(j+1) overwrites P_t(j): issued after PV_t(j), executed in order
@@ -445,22 +461,18 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
 #pragma unroll
       for (int i = 0; i < 4; i++) rsum2[i] = 0;
       constexpr int HALF = BN >= 64 ? 64 : BN;
+      static_assert(BN <= 64 || BN == 128, "at most two halves");
+      uint32_t un[BN == 128 ? 64 : 1];  // the second half's S columns, loaded ahead
 #pragma unroll
       for (int hbase = 0; hbase < BN; hbase += HALF) {
         float x[HALF];
         if (hbase == 0) {  // HALF == KEEP: the first (masked) columns from pass 1
 #pragma unroll
           for (int c = 0; c < HALF; c++) x[c] = xk[c];
-        } else {
-          {
-            uint32_t u[HALF];
+        } else {  // BN == 128: loaded at the end of the first half
+          tmem_ld_wait();
 #pragma unroll
-            for (int c = 0; c < HALF / 32; c++)
-              tmem_ld32(tS + hbase + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&u[c * 32]));
-            tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < HALF; c++) x[c] = __uint_as_float(u[c]);
-          }
+          for (int c = 0; c < HALF; c++) x[c] = __uint_as_float(un[c]);
           if (diag) {
 #pragma unroll
             for (int c = 0; c < HALF; c++)
@@ -516,6 +528,18 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
                 "r"(pl[6]), "r"(pl[7]), "r"(pl[8]), "r"(pl[9]), "r"(pl[10]), "r"(pl[11]),
                 "r"(pl[12]), "r"(pl[13]), "r"(pl[14]), "r"(pl[15])
                 : "memory");
+        }
+        if constexpr (BN == 128) {
+          if (hbase == 0) {
+            // load the second half now, then publish P's first half: the MMA
+            // thread runs PV over keys [0, 64) while this thread does the rest
+#pragma unroll
+            for (int c = 0; c < 2; c++)
+              tmem_ld32(tS + 64 + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&un[c * 32]));
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(bar(kP0Full0 + t * NSB + b));
+          }
         }
       }
       {
