@@ -291,10 +291,11 @@ class PrefillWork:
         self.gout = None
         if world > 1 and GATHER == "fused":
             # the attention kernel stores every rank's heads into every rank's
-            # `full` over NVLink; two device barriers per step (before, after)
+            # gathered output over NVLink (double-buffered: one device barrier
+            # per step)
             self.gout = GatheredOutput(S, self.H, hd, tdt, sh)
-            self.full = self.gout.full
-            self.launches_per_step = 5  # K/V prep, q prep, attention, 2 barriers
+            self.full = self.gout.bufs[0]
+            self.launches_per_step = 4  # K/V prep, q prep, attention, barrier
         elif world > 1:
             self.gath = torch.empty(world, S, self.Hl, hd, device="cuda", dtype=tdt)
             self.full = torch.empty(S, self.H, hd, device="cuda", dtype=tdt)
@@ -307,10 +308,10 @@ class PrefillWork:
     def step(self):
         eb = self.eb
         if self.gout is not None:
-            self.gout.barrier()
             eb.attention_prefill_gather(self.desc, self.layer, self.S, self.q, self.k, self.v,
-                                        self.kc, self.vc, self.gout.gather, self.ws)
+                                        self.kc, self.vc, self.gout.next(), self.ws)
             self.gout.barrier()
+            self.full = self.gout.full
             return
         eb.attention_prefill(self.desc, self.layer, self.S, self.q, self.k, self.v, self.kc,
                              self.vc, self.o, self.ws)
@@ -328,7 +329,8 @@ class PrefillWork:
         no barrier is needed between them."""
         if self.gout is not None:
             self.eb.attention_prefill_attend_gather(self.desc, self.layer, self.S, self.q,
-                                                    self.kc, self.vc, self.gout.gather, self.ws)
+                                                    self.kc, self.vc, self.gout.gathers[0],
+                                                    self.ws)
             return
         self.eb.attention_prefill_attend(self.desc, self.layer, self.S, self.q, self.kc, self.vc,
                                          self.o, self.ws)

@@ -66,14 +66,22 @@ def gather_heads(o_local, gath, full, world: int, rows: int, heads_per: int, hea
 
 class GatheredOutput:
     """The gathered [rows, n_heads, head_dim] output of a head-sharded prefill,
-    held in torch symmetric memory (mapped into every rank's address space)
-    so that eb_attention_prefill_gather can store each rank's heads into every
-    rank's copy. `gather` is the eb_head_gather for this rank's shard.
+    double-buffered in torch symmetric memory (mapped into every rank's
+    address space) so that eb_attention_prefill_gather can store each rank's
+    heads into every rank's copy.
 
-    Use: barrier(); eyebrowse_b200.attention_prefill_gather(..., gather);
-    barrier(). The first barrier keeps a rank from writing into a buffer a
-    peer is still reading; the second makes every rank's stores visible
-    before anyone reads `full`."""
+    Step i writes buffer i % 2 and ends with one cross-GPU barrier:
+
+        g = GatheredOutput(...)
+        gather = g.next()                  # eb_head_gather for this step
+        eyebrowse_b200.attention_prefill_gather(..., gather, ...)
+        g.barrier()                        # every rank's stores have landed
+        use(g.full)                        # this step's gathered output
+
+    One barrier per step is enough: a rank writes a buffer again only two
+    steps later, after every rank has passed the barrier of the step in
+    between, and so after every rank has finished reading it (reads are
+    stream-ordered before that next step's call)."""
 
     def __init__(self, rows: int, n_heads: int, head_dim: int, dtype, shard: HeadShard,
                  group=None):
@@ -84,13 +92,28 @@ class GatheredOutput:
 
         import eyebrowse_b200 as eb
         grp = group or dist.group.WORLD
-        self.full = symm_mem.empty(rows, n_heads, head_dim, dtype=dtype, device="cuda")
-        self.handle = symm_mem.rendezvous(self.full, grp.group_name)
+        self.bufs = symm_mem.empty(2, rows, n_heads, head_dim, dtype=dtype, device="cuda")
+        self.handle = symm_mem.rendezvous(self.bufs, grp.group_name)
         world, rank = self.handle.world_size, self.handle.rank
-        off = self.full.data_ptr() - self.handle.buffer_ptrs[rank]
-        self._dst = (ctypes.c_uint64 * world)(*[p + off for p in self.handle.buffer_ptrs])
-        self.gather = eb.HeadGather(n_dst=world, head_offset=shard.h0, n_heads_total=n_heads,
-                                    dst=ctypes.cast(self._dst, ctypes.POINTER(ctypes.c_uint64)))
+        base = self.bufs.data_ptr() - self.handle.buffer_ptrs[rank]
+        stride = self.bufs[1].data_ptr() - self.bufs[0].data_ptr()
+        self._dst = [(ctypes.c_uint64 * world)(*[p + base + i * stride
+                                                 for p in self.handle.buffer_ptrs])
+                     for i in range(2)]
+        self.gathers = [eb.HeadGather(n_dst=world, head_offset=shard.h0, n_heads_total=n_heads,
+                                      dst=ctypes.cast(d, ctypes.POINTER(ctypes.c_uint64)))
+                        for d in self._dst]
+        self.step = -1
+
+    def next(self):
+        """The eb_head_gather of the next step (alternating buffers)."""
+        self.step += 1
+        return self.gathers[self.step % 2]
+
+    @property
+    def full(self):
+        """The gathered output of the current step."""
+        return self.bufs[max(self.step, 0) % 2]
 
     def barrier(self):
         """Device-side barrier across the group's GPUs on the current stream."""

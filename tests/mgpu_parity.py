@@ -71,16 +71,16 @@ def main() -> int:
         ok &= ma <= 2e-3 and rl <= 1e-3
     # ---- the same prefill with the head gather fused into the kernel
     g = GatheredOutput(S, H, hd, f16, sh)
-    g.full.fill_(float("nan"))
+    g.bufs.fill_(float("nan"))
     g.barrier()
-    for _ in range(2):  # twice: the second call overwrites the first
-        g.barrier()
+    same = True
+    for _ in range(3):  # both buffers, and the first one again
         eb.attention_prefill_gather(desc, layer, S, dev(q[:, sh.h0:sh.h1]),
                                     dev(k[:, sh.kv0:sh.kv1]), dev(v[:, sh.kv0:sh.kv1]), kc, vc,
-                                    g.gather, ws)
+                                    g.next(), ws)
         g.barrier()
+        same &= torch.equal(g.full, full)
     torch.cuda.synchronize()
-    same = torch.equal(g.full, full)
     print(f"[mgpu] rank {rank} fused gather (TMA stores over NVLink) == NCCL gather: {same}",
           flush=True)
     ok &= same
