@@ -29,6 +29,7 @@
 // keeps ~21 mantissa bits on f16 tensor cores).
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -755,8 +756,23 @@ bool prefill_tc_supported(int hd) { return hd == 64 || hd == 128 || hd == 256; }
 cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* q16, const void* k16,
                               const void* v16, bool bf16, const void* split,
                               const GatherSpec* g, cudaStream_t st) {
-  // Two query tiles per CTA when the heads of a GQA group pair up.
-  const bool pair = ((a.H / a.Hkv) % 2) == 0;
+  // Two query tiles per CTA (the heads of a GQA pair share each K/V tile)
+  // when the group size is even and that is the faster grid. Causal query
+  // tiles differ in length (1 to n_qt KV tiles) and one CTA runs per SM, so
+  // a grid takes about max(its longest item, the average work per SM). A
+  // pair's longest item is twice a single head's, which decides it when the
+  // grid is small (a head-sharded rank with few heads); otherwise the pair
+  // wins, its per-head rate being ~1/0.87 of the one-tile kernel's
+  // (measured on config 3).
+  static int sms[32] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& n_sm = sms[dev & 31];
+  if (n_sm == 0) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  const double n_qt = (double)((a.S + 127) / 128);
+  const double per_sm = (double)a.H * n_qt * (n_qt + 1) / 2 / (n_sm > 0 ? n_sm : 148);
+  const bool pair = ((a.H / a.Hkv) % 2) == 0 &&
+                    std::max(2 * n_qt, per_sm) <= std::max(n_qt, per_sm) / 0.87;
   if (split) {
     switch (hd) {
       case 64:

@@ -36,8 +36,9 @@ def main() -> int:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", local))
     ok = True
-    # ---- prefill: config-3 geometry at S=1024 (f16)
-    S, H, Hkv, hd = 1024, 32, 8, 128
+    # ---- prefill: config-3 geometry at S=4608 (f16): with 16 heads per rank
+    # the grid is large enough for the two-tile (GQA pair) kernel
+    S, H, Hkv, hd = 4608, 32, 8, 128
     rng = np.random.default_rng(11)
     q = orc.round_f16(rng.standard_normal((S, H, hd)).astype(np.float32) * 0.5).reshape(S, H, hd)
     k = orc.round_f16(rng.standard_normal((S, Hkv, hd)).astype(np.float32) * 0.5).reshape(S, Hkv, hd)
