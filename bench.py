@@ -250,9 +250,18 @@ class PrefillWork:
                 "scale": round(self.scale, 6), "qk_norm": self.qk_norm, "v_norm": self.v_norm,
                 "rope_angles": self.rope_angles or self.hd // 2, "batch": 1,
                 "parallelism": f"heads/{world}" if world > 1 else "1 GPU",
-                "head_concat": ("fused: the attention kernel TMA-stores each output tile "
-                                "into every rank's buffer over NVLink" if GATHER == "fused"
-                                else "NCCL all-gather + eb_head_concat") if world > 1 else None}
+                "head_concat": self._concat_desc(world)}
+
+    def _concat_desc(self, world):
+        if world == 1:
+            return None
+        if GATHER != "fused":
+            return "NCCL all-gather + eb_head_concat"
+        g = getattr(self, "gout", None)
+        if g is not None and g.mode == "multicast":
+            return ("own-buffer write + eb_head_broadcast through the NVLink multicast "
+                    "address (multimem)")
+        return "fused: the attention kernel TMA-stores each output tile into every rank's buffer"
 
     def setup(self, rank, world):
         import torch
@@ -295,7 +304,8 @@ class PrefillWork:
             # per step)
             self.gout = GatheredOutput(S, self.H, hd, tdt, sh)
             self.full = self.gout.bufs[0]
-            self.launches_per_step = 4  # K/V prep, q prep, attention, barrier
+            # K/V prep, q prep, attention, barrier (+ the multicast broadcast)
+            self.launches_per_step = 4 + (1 if self.gout.mode == "multicast" else 0)
         elif world > 1:
             self.gath = torch.empty(world, S, self.Hl, hd, device="cuda", dtype=tdt)
             self.full = torch.empty(S, self.H, hd, device="cuda", dtype=tdt)
@@ -310,7 +320,7 @@ class PrefillWork:
         if self.gout is not None:
             eb.attention_prefill_gather(self.desc, self.layer, self.S, self.q, self.k, self.v,
                                         self.kc, self.vc, self.gout.next(), self.ws)
-            self.gout.barrier()
+            self.gout.finish()
             self.full = self.gout.full
             return
         eb.attention_prefill(self.desc, self.layer, self.S, self.q, self.k, self.v, self.kc,

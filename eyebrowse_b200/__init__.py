@@ -28,7 +28,7 @@ EXPORTS = (
     "eb_attention_prefill_gather", "eb_attention_prefill_attend_gather",
     "eb_attention_decode", "eb_attention_decode_batched", "eb_attention_decode_workspace_bytes",
     "eb_workspace_init", "eb_head_concat", "eb_get_device_error",
-    "eb_attention_decode_noalloc",
+    "eb_attention_decode_noalloc", "eb_head_broadcast",
 )
 
 
@@ -92,6 +92,8 @@ def lib() -> ctypes.CDLL:
     L.eb_attention_prefill.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
     L.eb_attention_prefill_kv.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
     L.eb_attention_prefill_attend.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
+    L.eb_head_broadcast.argtypes = [_vp, _vp, _i64, _i64, ctypes.c_int32, ctypes.c_int32, _i64,
+                                    ctypes.c_int32, _vp]
     gp = ctypes.POINTER(HeadGather)
     L.eb_attention_prefill_gather.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, gp, _vp, _sz,
                                               _vp]
@@ -256,6 +258,15 @@ def attention_prefill_attend_gather(desc, layer, seq, q, kcache, vcache, gather:
                                                     ctypes.byref(gather), _ptr(workspace),
                                                     ws_bytes, _stream(stream)),
            "eb_attention_prefill_attend_gather")
+
+
+def head_broadcast(local, multicast_ptr: int, rows, n_heads_total, head_offset, n_heads,
+                   head_dim, dtype, stream=None):
+    """eb_head_broadcast: this rank's heads of `local` into every rank's buffer
+    through the multicast address."""
+    _check(lib().eb_head_broadcast(_ptr(local), multicast_ptr, rows, n_heads_total, head_offset,
+                                   n_heads, head_dim, dtype, _stream(stream)),
+           "eb_head_broadcast")
 
 
 def attention_decode_workspace_bytes(desc, batch, max_pos) -> int:

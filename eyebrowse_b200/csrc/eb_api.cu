@@ -663,6 +663,21 @@ int eb_head_concat(const void* src, void* dst, int64_t shards, int64_t rows, int
                                         elem_bytes(dtype), reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int eb_head_broadcast(const void* local, void* multicast, int64_t rows, int64_t n_heads_total,
+                      int32_t head_offset, int32_t n_heads, int64_t head_dim, int32_t dtype,
+                      eb_stream_t stream) {
+  if (!local || !multicast || rows < 0 || n_heads_total <= 0 || head_offset < 0 || n_heads <= 0 ||
+      head_offset + n_heads > n_heads_total || head_dim <= 0 || !dtype_ok(dtype))
+    return EB_ERR_INVALID_ARGUMENT;
+  const int es = elem_bytes(dtype);
+  if (((head_dim * es) & 15) || !aligned16(local) || !aligned16(multicast))
+    return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  return cuda_status(launch_head_broadcast(local, multicast, rows, n_heads_total, head_offset,
+                                           n_heads, head_dim, es,
+                                           reinterpret_cast<cudaStream_t>(stream)));
+}
+
 int eb_get_device_error(uint32_t* bits) {
   if (!bits) return EB_ERR_INVALID_ARGUMENT;
   unsigned* p = error_word_ptr();

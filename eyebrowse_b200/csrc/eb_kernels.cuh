@@ -19,6 +19,9 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float* out, int64_t r
                            float eps, cudaStream_t st);
 cudaError_t launch_head_concat(const void* src, void* dst, int64_t shards, int64_t rows,
                                int64_t heads_per, int64_t hd, int elem_bytes, cudaStream_t st);
+cudaError_t launch_head_broadcast(const void* local, void* mc, int64_t rows, int64_t h_total,
+                                  int64_t h0, int64_t nh, int64_t hd, int elem_bytes,
+                                  cudaStream_t st);
 
 // K/V preparation for a run of rows: k -> RMSNorm(k_norm_w) -> RoPE(row pos0+r),
 // v -> RMSNorm(v_norm_w); written to the cache rows [dst0, dst0+rows) in the

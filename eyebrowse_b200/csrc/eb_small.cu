@@ -151,6 +151,41 @@ cudaError_t launch_head_concat(const void* src, void* dst, int64_t shards, int64
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- head broadcast
+// Rows x heads [h0, h0 + nh) of a gathered [rows][H][hd] buffer, stored through
+// an NVLink multicast address (multimem.st): the switch writes every 16-byte
+// word to the same offset of each GPU's buffer bound to the multicast object,
+// so each word leaves this GPU once whatever the number of GPUs.
+__global__ void head_broadcast_kernel(const char* __restrict__ src, char* mc, int64_t rows,
+                                      int64_t row_bytes, int64_t off_bytes, int64_t span16) {
+  const int64_t total = rows * span16;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / span16, u = i - r * span16;
+    const int64_t o = r * row_bytes + off_bytes + u * 16;
+    const uint4 v = *reinterpret_cast<const uint4*>(src + o);
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc + o),
+                 "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+                 "f"(__uint_as_float(v.w))
+                 : "memory");
+  }
+}
+
+cudaError_t launch_head_broadcast(const void* local, void* mc, int64_t rows, int64_t h_total,
+                                  int64_t h0, int64_t nh, int64_t hd, int elem_bytes,
+                                  cudaStream_t st) {
+  const int64_t span16 = nh * hd * elem_bytes / 16;
+  if (rows == 0 || span16 == 0) return cudaSuccess;
+  const int64_t total = rows * span16;
+  const int threads = 512;
+  int64_t blocks = (total + threads - 1) / threads;
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  head_broadcast_kernel<<<(unsigned)blocks, threads, 0, st>>>(
+      static_cast<const char*>(local), static_cast<char*>(mc), rows, h_total * hd * elem_bytes,
+      h0 * hd * elem_bytes, span16);
+  return cudaGetLastError();
+}
+
 // ---------------------------------------------------------------- K/V prep
 // One warp per (sequence, row, kv head, k|v). The row is staged in shared
 // memory, transformed with the reference's op order (norm, then RoPE for k;

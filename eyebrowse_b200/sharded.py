@@ -9,7 +9,9 @@ boundary in one of two ways:
   - GatheredOutput + eb_attention_prefill_gather: the attention kernel stores
     every finished output tile straight into every rank's [rows, H, hd]
     buffer over NVLink (TMA stores into peer memory) while the rest of the
-    kernel runs; no separate collective runs.
+    kernel runs; or, from 8 GPUs, it writes its own buffer and
+    eb_head_broadcast sends its heads once through an NVLink multicast
+    address. No library collective runs.
   - gather_heads: NCCL all-gather into [G, rows, H/G, hd], then
     eb_head_concat restores [rows, H, hd] (the library-collective baseline).
 """
@@ -66,16 +68,28 @@ def gather_heads(o_local, gath, full, world: int, rows: int, heads_per: int, hea
 
 class GatheredOutput:
     """The gathered [rows, n_heads, head_dim] output of a head-sharded prefill,
-    double-buffered in torch symmetric memory (mapped into every rank's
-    address space) so that eb_attention_prefill_gather can store each rank's
-    heads into every rank's copy.
+    double-buffered in torch symmetric memory (every rank's buffers mapped
+    into every process; torch allocates, maps and provides the device
+    barrier, the stores are this library's). Two ways to fill it:
 
-    Step i writes buffer i % 2 and ends with one cross-GPU barrier:
+      mode "peer":      the attention kernel TMA-stores each finished output
+                        tile into all ranks' buffers over NVLink, overlapped
+                        with the rest of the kernel (each word leaves the GPU
+                        world - 1 times);
+      mode "multicast": the attention kernel writes this rank's heads into
+                        its own buffer, then eb_head_broadcast sends them once
+                        through the buffers' NVLink multicast address and the
+                        switch writes every rank's copy (each word leaves once);
+      mode "auto":      multicast from 8 GPUs up when the GPUs support it
+                        (measured: peer stores reach ~600 GB/s per GPU,
+                        multimem stores ~330 GB/s, so the single copy wins
+                        once world - 1 copies outweigh the overlap), else peer.
 
-        g = GatheredOutput(...)
+    Step i writes buffer i % 2:
+
         gather = g.next()                  # eb_head_gather for this step
         eyebrowse_b200.attention_prefill_gather(..., gather, ...)
-        g.barrier()                        # every rank's stores have landed
+        g.finish()                         # broadcast (multicast mode), barrier
         use(g.full)                        # this step's gathered output
 
     One barrier per step is enough: a rank writes a buffer again only two
@@ -84,25 +98,42 @@ class GatheredOutput:
     stream-ordered before that next step's call)."""
 
     def __init__(self, rows: int, n_heads: int, head_dim: int, dtype, shard: HeadShard,
-                 group=None):
+                 group=None, mode: str = "auto"):
         import ctypes
 
+        import torch
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
+        from torch._C._distributed_c10d import _SymmetricMemory
 
         import eyebrowse_b200 as eb
         grp = group or dist.group.WORLD
+        self.eb, self.shard, self.rows, self.n_heads, self.hd = eb, shard, rows, n_heads, head_dim
+        self.dtype_code = {torch.float32: eb.EB_F32, torch.float16: eb.EB_F16,
+                           torch.bfloat16: eb.EB_BF16}[dtype]
         self.bufs = symm_mem.empty(2, rows, n_heads, head_dim, dtype=dtype, device="cuda")
         self.handle = symm_mem.rendezvous(self.bufs, grp.group_name)
         world, rank = self.handle.world_size, self.handle.rank
         base = self.bufs.data_ptr() - self.handle.buffer_ptrs[rank]
-        stride = self.bufs[1].data_ptr() - self.bufs[0].data_ptr()
-        self._dst = [(ctypes.c_uint64 * world)(*[p + base + i * stride
-                                                 for p in self.handle.buffer_ptrs])
+        self.stride = self.bufs[1].data_ptr() - self.bufs[0].data_ptr()
+        has_mc = bool(_SymmetricMemory.has_multicast_support(
+            torch._C._autograd.DeviceType.CUDA, torch.cuda.current_device())
+            and self.handle.multicast_ptr)
+        if mode == "auto":
+            mode = "multicast" if (has_mc and world >= 8) else "peer"
+        if mode == "multicast" and not has_mc:
+            raise RuntimeError("NVLink multicast is not supported on these GPUs")
+        self.mode = mode
+        self.mc = self.handle.multicast_ptr + base if mode == "multicast" else 0
+        if mode == "multicast":
+            addrs = [[self.bufs[i].data_ptr()] for i in range(2)]
+        else:
+            addrs = [[p + base + i * self.stride for p in self.handle.buffer_ptrs]
                      for i in range(2)]
-        self.gathers = [eb.HeadGather(n_dst=world, head_offset=shard.h0, n_heads_total=n_heads,
+        self._dst = [(ctypes.c_uint64 * len(a))(*a) for a in addrs]
+        self.gathers = [eb.HeadGather(n_dst=len(a), head_offset=shard.h0, n_heads_total=n_heads,
                                       dst=ctypes.cast(d, ctypes.POINTER(ctypes.c_uint64)))
-                        for d in self._dst]
+                        for a, d in zip(addrs, self._dst)]
         self.step = -1
 
     def next(self):
@@ -114,6 +145,16 @@ class GatheredOutput:
     def full(self):
         """The gathered output of the current step."""
         return self.bufs[max(self.step, 0) % 2]
+
+    def finish(self):
+        """After this rank's attention call: in multicast mode, send this
+        rank's heads to every rank; then the cross-GPU barrier."""
+        if self.mode == "multicast":
+            i = max(self.step, 0) % 2
+            self.eb.head_broadcast(self.bufs[i], self.mc + i * self.stride, self.rows,
+                                   self.n_heads, self.shard.h0, self.shard.n_heads, self.hd,
+                                   self.dtype_code)
+        self.barrier()
 
     def barrier(self):
         """Device-side barrier across the group's GPUs on the current stream."""

@@ -254,6 +254,19 @@ EB_API int eb_attention_decode_noalloc(const eb_attn_desc* desc, const eb_attn_l
 EB_API int eb_head_concat(const void* src, void* dst, int64_t shards, int64_t rows, int64_t heads_per,
                    int64_t head_dim, int32_t dtype, eb_stream_t stream);
 
+/* The other exchange at the head-concat boundary, for many GPUs: copies rows
+ * x heads [head_offset, head_offset + n_heads) of this rank's gathered buffer
+ * `local` [rows, n_heads_total, head_dim] through `multicast`, an NVLink
+ * multicast address bound to every rank's gathered buffer (same offsets):
+ * each 16-byte word leaves this GPU once (multimem.st) and the switch writes
+ * it into every rank's buffer. A rank first writes its own heads into its
+ * own buffer (eb_attention_prefill_gather with n_dst = 1), then calls this;
+ * the same barriers as for eb_attention_prefill_gather apply.
+ * head_dim * element size must be a multiple of 16 bytes. */
+EB_API int eb_head_broadcast(const void* local, void* multicast, int64_t rows,
+                             int64_t n_heads_total, int32_t head_offset, int32_t n_heads,
+                             int64_t head_dim, int32_t dtype, eb_stream_t stream);
+
 /* Returns and clears the device-side error word of the current device: a
  * non-zero value means some kernel's bounded wait gave up (the kernel then
  * returned early and its output is invalid). Synchronises the device. */

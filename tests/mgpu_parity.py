@@ -9,8 +9,9 @@ on every rank over NCCL (eyebrowse_b200.sharded.gather_heads). Rank 0 checks
 the full result against the oracle at max-abs <= 2e-3, rel-L2 <= 1e-3. The
 prefill then runs again with the gather fused into the attention kernel
 (eb_attention_prefill_gather: TMA stores into every rank's symmetric-memory
-buffer), and every rank checks that its gathered copy equals the NCCL
-result bit for bit. Exits non-zero on
+buffer), and with own-buffer writes followed by eb_head_broadcast through
+the NVLink multicast address; every rank checks that its gathered copy
+equals the NCCL result bit for bit. Exits non-zero on
 any mismatch. Not collected by pytest: it needs N processes.
 """
 import datetime
@@ -70,22 +71,28 @@ def main() -> int:
         print(f"[mgpu] world={world} prefill rows [{S-96},{S}) x {H} heads: max_abs={ma:.2e} "
               f"rel_l2={rl:.2e}", flush=True)
         ok &= ma <= 2e-3 and rl <= 1e-3
-    # ---- the same prefill with the head gather fused into the kernel
-    g = GatheredOutput(S, H, hd, f16, sh)
-    g.bufs.fill_(float("nan"))
-    g.barrier()
-    same = True
-    for _ in range(3):  # both buffers, and the first one again
-        eb.attention_prefill_gather(desc, layer, S, dev(q[:, sh.h0:sh.h1]),
-                                    dev(k[:, sh.kv0:sh.kv1]), dev(v[:, sh.kv0:sh.kv1]), kc, vc,
-                                    g.next(), ws)
+    # ---- the same prefill with the gather fused into the kernel (peer TMA
+    # stores), and with own-buffer writes + the multicast broadcast
+    for mode in ("peer", "multicast"):
+        try:
+            g = GatheredOutput(S, H, hd, f16, sh, mode=mode)
+        except RuntimeError as e:
+            if rank == 0:
+                print(f"[mgpu] {mode}: {e}", flush=True)
+            continue
+        g.bufs.fill_(float("nan"))
         g.barrier()
-        same &= torch.equal(g.full, full)
-    torch.cuda.synchronize()
-    print(f"[mgpu] rank {rank} fused gather (TMA stores over NVLink) == NCCL gather: {same}",
-          flush=True)
-    ok &= same
-    del g
+        same = True
+        for _ in range(3):  # both buffers, and the first one again
+            eb.attention_prefill_gather(desc, layer, S, dev(q[:, sh.h0:sh.h1]),
+                                        dev(k[:, sh.kv0:sh.kv1]), dev(v[:, sh.kv0:sh.kv1]), kc,
+                                        vc, g.next(), ws)
+            g.finish()
+            same &= torch.equal(g.full, full)
+        torch.cuda.synchronize()
+        print(f"[mgpu] rank {rank} gathered output ({mode}) == NCCL gather: {same}", flush=True)
+        ok &= same
+        del g
     # ---- batched decode: config-5 geometry, 8 sequences, f16 caches
     B, max_seq = 8, 4096
     pos = (np.random.default_rng(12).integers(512, max_seq, size=B) - 1).astype(np.int32)
