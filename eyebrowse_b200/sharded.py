@@ -80,10 +80,12 @@ class GatheredOutput:
                         its own buffer, then eb_head_broadcast sends them once
                         through the buffers' NVLink multicast address and the
                         switch writes every rank's copy (each word leaves once);
-      mode "auto":      multicast from 8 GPUs up when the GPUs support it
-                        (measured: peer stores reach ~600 GB/s per GPU,
-                        multimem stores ~330 GB/s, so the single copy wins
-                        once world - 1 copies outweigh the overlap), else peer.
+      mode "auto":      peer. Measured on B200 (config 3, S=8192): at 2 GPUs
+                        peer stores add ~5 us to the kernel; at 8 GPUs the
+                        peer step takes 0.167-0.177 ms and the multicast step
+                        0.201 ms. A streaming multimem.st kernel reaches ~330
+                        GB/s per sender with 2 GPUs in the multicast group but
+                        ~80 GB/s with 8, so the single copy does not win.
 
     Step i writes buffer i % 2:
 
@@ -120,7 +122,7 @@ class GatheredOutput:
             torch._C._autograd.DeviceType.CUDA, torch.cuda.current_device())
             and self.handle.multicast_ptr)
         if mode == "auto":
-            mode = "multicast" if (has_mc and world >= 8) else "peer"
+            mode = "peer"
         if mode == "multicast" and not has_mc:
             raise RuntimeError("NVLink multicast is not supported on these GPUs")
         self.mode = mode
