@@ -71,7 +71,10 @@ static DecodePlan plan_decode(int64_t batch, int64_t h, int64_t hkv, int64_t hd,
     return p;
   }
   const int rpb = decode_rows_per_batch((int)hd, dtype_cache, (int)(h / hkv));
-  const int64_t target_ctas = 2 * 148;
+#ifndef EB_DECODE_CTAS_PER_SM
+#define EB_DECODE_CTAS_PER_SM 2
+#endif
+  const int64_t target_ctas = EB_DECODE_CTAS_PER_SM * 148;
   int64_t chunk = (rows * batch * hkv + target_ctas - 1) / target_ctas;
   chunk = (chunk + rpb - 1) / rpb * rpb;
   if (chunk < rpb) chunk = rpb;

@@ -244,25 +244,38 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
   if (!sm_last) return;
   __threadfence();
   float* wts = work;  // [G][MAXC], reuses the slot accumulators
-  if (tid < G) {
-    const float* ml = a.ws_ml + (((int64_t)b * a.H + head0 + tid) * a.cmax) * 2;
+  // One warp per head: lanes over the chunks for the max, the chunk weights
+  // 2^(m_c - M) and the row sum (the partials are read in parallel, not by one
+  // thread in a dependent loop).
+  for (int g = warp; g < G; g += kDecWarps) {
+    const float* ml = a.ws_ml + (((int64_t)b * a.H + head0 + g) * a.cmax) * 2;
     float M = -INFINITY;
-    for (int cc = 0; cc < n_chunks; cc++) M = fmaxf(M, __ldcg(ml + 2 * cc));
+    for (int cc = lane; cc < n_chunks; cc += 32) M = fmaxf(M, __ldcg(ml + 2 * cc));
+    M = warp_max(M);
     float L = 0.f;
-    for (int cc = 0; cc < n_chunks; cc++) {
+    for (int cc = lane; cc < n_chunks; cc += 32) {
       const float w = ex2(__ldcg(ml + 2 * cc) - M);
-      wts[tid * MAXC + cc] = w;
+      wts[g * MAXC + cc] = w;
       L += __ldcg(ml + 2 * cc + 1) * w;
     }
-    sm_L[tid] = L;
+    L = warp_sum(L);
+    if (lane == 0) sm_L[g] = L;
   }
   __syncthreads();
   for (int idx = tid; idx < G * HD; idx += kDecWarps * 32) {
     const int g = idx / HD, d = idx % HD;
     const int h = head0 + g;
     const float* pa = a.ws_acc + (((int64_t)b * a.H + h) * a.cmax) * HD + d;
-    float O = 0.f;
-    for (int cc = 0; cc < n_chunks; cc++) O += __ldcg(pa + (int64_t)cc * HD) * wts[g * MAXC + cc];
+    const float* wg = wts + g * MAXC;
+    // 8 independent sums: 8 partial loads in flight per thread
+    float O8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int cc = 0;
+    for (; cc + 8 <= n_chunks; cc += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; u++) O8[u] += __ldcg(pa + (int64_t)(cc + u) * HD) * wg[cc + u];
+    }
+    for (; cc < n_chunks; cc++) O8[0] += __ldcg(pa + (int64_t)cc * HD) * wg[cc];
+    const float O = ((O8[0] + O8[1]) + (O8[2] + O8[3])) + ((O8[4] + O8[5]) + (O8[6] + O8[7]));
     st_any(a.o, (int64_t)b * a.o_bstride + (int64_t)h * HD + d, a.dtype_o, O / sm_L[g]);
   }
   if (tid == 0) *cnt = 0u;

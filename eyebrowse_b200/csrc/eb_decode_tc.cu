@@ -424,22 +424,40 @@ __global__ void __launch_bounds__(96)
         if (lane == 0) ticket = atomicAdd(cnt, 1u);
         ticket = __shfl_sync(0xffffffffu, ticket, 0);
         if (ticket == (unsigned)(n_chunks - 1)) {
-          // last CTA of this (sequence, head group): merge the chunk partials
+          // last CTA of this (sequence, head group): merge the chunk partials.
+          // Per head: lanes over the chunks for the max and the weights
+          // 2^(m_c - M), which go to the K/V ring (idle now: every MMA has
+          // completed and every TMA load has landed); then each lane sums its
+          // columns over the chunks with 8 partial loads in flight.
           __threadfence();
+          float* wts = reinterpret_cast<float*>(smem + C::Q_BYTES);  // [n_chunks <= 256]
           for (int g = 0; g < G; g++) {
             const int hh = head0 + g;
             const float* mlg = a.ws_ml + (((int64_t)b * a.H + hh) * a.cmax) * 2;
             float M = -INFINITY;
-            for (int k = 0; k < n_chunks; k++) M = fmaxf(M, __ldcg(mlg + 2 * k));
+            for (int k = lane; k < n_chunks; k += 32) M = fmaxf(M, __ldcg(mlg + 2 * k));
+            M = warp_max(M);
             float L = 0.f;
-            for (int k = 0; k < n_chunks; k++) L += __ldcg(mlg + 2 * k + 1) * ex2(__ldcg(mlg + 2 * k) - M);
+            for (int k = lane; k < n_chunks; k += 32) {
+              const float w = ex2(__ldcg(mlg + 2 * k) - M);
+              wts[k] = w;
+              L += __ldcg(mlg + 2 * k + 1) * w;
+            }
+            L = warp_sum(L);
+            __syncwarp();
             const float* accg = a.ws_acc + (((int64_t)b * a.H + hh) * a.cmax) * HD;
             for (int d = lane; d < HD; d += 32) {
-              float O = 0.f;
-              for (int k = 0; k < n_chunks; k++)
-                O += __ldcg(accg + (int64_t)k * HD + d) * ex2(__ldcg(mlg + 2 * k) - M);
+              float O8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+              int k = 0;
+              for (; k + 8 <= n_chunks; k += 8) {
+#pragma unroll
+                for (int u = 0; u < 8; u++) O8[u] += __ldcg(accg + (int64_t)(k + u) * HD + d) * wts[k + u];
+              }
+              for (; k < n_chunks; k++) O8[0] += __ldcg(accg + (int64_t)k * HD + d) * wts[k];
+              const float O = ((O8[0] + O8[1]) + (O8[2] + O8[3])) + ((O8[4] + O8[5]) + (O8[6] + O8[7]));
               st_any(a.o, (int64_t)b * a.o_bstride + (int64_t)hh * HD + d, a.dtype_o, O / L);
             }
+            __syncwarp();  // wts is rewritten for the next head
           }
           if (lane == 0) *cnt = 0u;
         }
