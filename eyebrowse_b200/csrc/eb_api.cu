@@ -3,6 +3,7 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/eyebrowse_attn.h"
@@ -61,6 +62,20 @@ struct DecodePlan {
   size_t cnt_off, ml_off, acc_off, bytes;
 };
 
+#ifndef EB_DECODE_CTAS_PER_SM
+#define EB_DECODE_CTAS_PER_SM 2
+#endif
+static constexpr int64_t kDecodeTargetCtas = EB_DECODE_CTAS_PER_SM * 148;
+
+// Split-K workspace layout for p.cmax chunks: combine tickets, then the
+// per-chunk (max, sum) pairs, then the per-chunk partial outputs.
+static void decode_layout(DecodePlan& p, int64_t batch, int64_t h, int64_t hd) {
+  p.cnt_off = 0;
+  p.ml_off = round_up((size_t)batch * h * sizeof(unsigned));
+  p.acc_off = p.ml_off + round_up((size_t)batch * h * p.cmax * 2 * sizeof(float));
+  p.bytes = p.acc_off + round_up((size_t)batch * h * p.cmax * hd * sizeof(float));
+}
+
 static DecodePlan plan_decode(int64_t batch, int64_t h, int64_t hkv, int64_t hd, int dtype_cache,
                               int64_t max_pos) {
   DecodePlan p{};
@@ -71,10 +86,7 @@ static DecodePlan plan_decode(int64_t batch, int64_t h, int64_t hkv, int64_t hd,
     return p;
   }
   const int rpb = decode_rows_per_batch((int)hd, dtype_cache, (int)(h / hkv));
-#ifndef EB_DECODE_CTAS_PER_SM
-#define EB_DECODE_CTAS_PER_SM 2
-#endif
-  const int64_t target_ctas = EB_DECODE_CTAS_PER_SM * 148;
+  const int64_t target_ctas = kDecodeTargetCtas;
   int64_t chunk = (rows * batch * hkv + target_ctas - 1) / target_ctas;
   chunk = (chunk + rpb - 1) / rpb * rpb;
   if (chunk < rpb) chunk = rpb;
@@ -88,11 +100,31 @@ static DecodePlan plan_decode(int64_t batch, int64_t h, int64_t hkv, int64_t hd,
   }
   p.chunk = (int)chunk;
   p.cmax = (int)((rows + chunk - 1) / chunk);
-  p.cnt_off = 0;
-  p.ml_off = round_up((size_t)batch * h * sizeof(unsigned));
-  p.acc_off = p.ml_off + round_up((size_t)batch * h * p.cmax * 2 * sizeof(float));
-  p.bytes = p.acc_off + round_up((size_t)batch * h * p.cmax * hd * sizeof(float));
+  decode_layout(p, batch, h, hd);
   return p;
+}
+
+// Workspace that covers plan_decode for EVERY context of 1..max_pos+1 rows.
+// The chunk count is not monotonic in the context length (rounding the chunk
+// up to whole row batches can give a shorter context more chunks), so the
+// size comes from a bound on it instead of the plan at max_pos: the chunk is
+// at least rows*batch*hkv/target_ctas unless capped at 8192 rows, at least
+// rows/256, and at least one row batch.
+static size_t decode_workspace_bound(int64_t batch, int64_t h, int64_t hkv, int64_t hd,
+                                     int dtype_cache, int64_t max_pos) {
+  if (hd != 64 && hd != 128 && hd != 256) return 0;
+  const int64_t rows = max_pos + 1;
+  const int64_t rpb = decode_rows_per_batch((int)hd, dtype_cache, (int)(h / hkv));
+  const int64_t bh = batch * hkv;
+  int64_t c = (kDecodeTargetCtas + bh - 1) / bh;
+  c = std::max<int64_t>(c, (rows + 8191) / 8192);
+  c = std::min<int64_t>(c, 256);
+  c = std::min<int64_t>(c, (rows + rpb - 1) / rpb);
+  if (c <= 1) return 0;
+  DecodePlan p{};
+  p.cmax = (int)c;
+  decode_layout(p, batch, h, hd);
+  return p.bytes;
 }
 
 static bool desc_ok(const eb_attn_desc* d) {
@@ -112,6 +144,11 @@ static int64_t kvs_of(const eb_attn_desc* d) {
 }
 static int64_t os_of(const eb_attn_desc* d) {
   return d->o_stride ? d->o_stride : (int64_t)d->n_heads * d->head_dim;
+}
+
+size_t decode_plan_bytes(const eb_attn_desc* d, int64_t batch, int64_t max_pos) {
+  return plan_decode(batch, d->n_heads, d->n_kv_heads, d->head_dim, d->dtype_cache, max_pos)
+      .bytes;
 }
 
 // Shared body of single and batched decode (also used by eb_noalloc.cu).
@@ -340,7 +377,7 @@ int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, in
 
 size_t eb_attn_decode_workspace_bytes(int64_t h, int64_t hkv, int64_t pos, int64_t hd) {
   if (h <= 0 || hkv <= 0 || pos < 0) return 0;
-  return plan_decode(1, h, hkv, hd, kF32, pos).bytes;
+  return decode_workspace_bound(1, h, hkv, hd, kF32, pos);
 }
 
 int eb_attn_decode(const float* q, const float* kcache, const float* vcache, float* o, int64_t h,
@@ -617,7 +654,8 @@ int eb_attention_prefill(const eb_attn_desc* d, const eb_attn_layer* L, int64_t 
 size_t eb_attention_decode_workspace_bytes(const eb_attn_desc* d, int64_t batch,
                                            int64_t max_pos) {
   if (!desc_ok(d) || batch <= 0 || max_pos < 0) return 0;
-  return plan_decode(batch, d->n_heads, d->n_kv_heads, d->head_dim, d->dtype_cache, max_pos).bytes;
+  return decode_workspace_bound(batch, d->n_heads, d->n_kv_heads, d->head_dim, d->dtype_cache,
+                                max_pos);
 }
 
 int eb_attention_decode(const eb_attn_desc* d, const eb_attn_layer* L, int64_t pos,

@@ -20,7 +20,16 @@
 namespace eb {
 
 constexpr int kDecWarps = 4;
-constexpr int kDecU = 4;  // row steps loaded per batch, all loads issued before use
+// Row steps loaded per batch, all loads issued before use: 8 for an f32 cache
+// whose row a lane holds in one 16-byte load (64 registers of K/V in
+// flight), else 4 (16-bit rows carry twice the elements per load, and with
+// 8 query heads per CTA more steps would spill).
+#ifndef EB_DECODE_U1
+#define EB_DECODE_U1 8
+#endif
+constexpr int dec_steps(int loads, int elem_bytes) {
+  return (loads == 1 && elem_bytes == 4) ? EB_DECODE_U1 : 4;
+}
 
 template <int HD, typename TC>
 struct DecShape {
@@ -31,7 +40,8 @@ struct DecShape {
   static constexpr int RPW = 32 / LPR;                       // rows per warp step
   static constexpr int EPL = VEC * LOADS;                    // elements per lane per row
   static constexpr int NS = kDecWarps * RPW;                 // softmax state slots per CTA
-  static constexpr int ROWS_PER_BATCH = kDecWarps * RPW * kDecU;
+  static constexpr int U = dec_steps(LOADS, (int)sizeof(TC));
+  static constexpr int ROWS_PER_BATCH = kDecWarps * RPW * U;
 };
 
 template <typename TC, int N>
@@ -128,10 +138,10 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
                  (int64_t)kvh * HD + sl * VEC;
 
   for (int r0 = row_begin; r0 < row_end; r0 += Sh::ROWS_PER_BATCH) {
-    uint4 kr[kDecU][LOADS], vr[kDecU][LOADS];
-    bool ok[kDecU];
+    uint4 kr[Sh::U][LOADS], vr[Sh::U][LOADS];
+    bool ok[Sh::U];
 #pragma unroll
-    for (int u = 0; u < kDecU; u++) {
+    for (int u = 0; u < Sh::U; u++) {
       const int row = r0 + (u * kDecWarps + warp) * RPW + slot;
       ok[u] = row < row_end;
 #pragma unroll
@@ -145,9 +155,9 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
         }
       }
     }
-    float s[kDecU][G];
+    float s[Sh::U][G];
 #pragma unroll
-    for (int u = 0; u < kDecU; u++) {
+    for (int u = 0; u < Sh::U; u++) {
       float kf[EPL];
       unpack<TC, LOADS>(kr[u], kf);
 #pragma unroll
@@ -164,7 +174,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
     for (int g = 0; g < G; g++) {
       float mb = s[0][g];
 #pragma unroll
-      for (int u = 1; u < kDecU; u++) mb = fmaxf(mb, s[u][g]);
+      for (int u = 1; u < Sh::U; u++) mb = fmaxf(mb, s[u][g]);
       if (mb == -INFINITY) continue;
       const float mn = fmaxf(m[g], mb);
       const float corr = ex2(m[g] - mn);
@@ -174,7 +184,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
       m[g] = mn;
     }
 #pragma unroll
-    for (int u = 0; u < kDecU; u++) {
+    for (int u = 0; u < Sh::U; u++) {
       float vf[EPL];
       unpack<TC, LOADS>(vr[u], vf);
 #pragma unroll
@@ -284,10 +294,11 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
 int decode_rows_per_batch(int hd, int dtype_cache, int group) {
   if (decode_tc_supported(hd, dtype_cache, group)) return 64;  // tensor-core tile rows
   const int vec = dtype_cache == kF32 ? 4 : 8;
-  int lpr = hd / vec;
-  if (lpr > 32) lpr = 32;
+  const int lpr_raw = hd / vec;
+  const int lpr = lpr_raw > 32 ? 32 : lpr_raw;
+  const int loads = lpr_raw >= 32 ? lpr_raw / 32 : 1;
   const int rpw = 32 / lpr;
-  return kDecWarps * rpw * kDecU;
+  return kDecWarps * rpw * dec_steps(loads, dtype_cache == kF32 ? 4 : 2);
 }
 
 template <int HD, typename TC>

@@ -119,6 +119,9 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
                 const void* k, const void* v, void* kc, void* vc, int64_t cache_bstride, void* o,
                 int64_t q_bstride, int64_t kv_bstride, int64_t o_bstride, void* ws, size_t ws_bytes,
                 cudaStream_t st);
+// Workspace bytes the split-K plan of one decode call at max_pos needs (0 when
+// it does not split), defined in eb_api.cu.
+size_t decode_plan_bytes(const eb_attn_desc* d, int64_t batch, int64_t max_pos);
 
 // ------------------------------------------------------------- prefill (tcgen05)
 struct PrefillArgs {

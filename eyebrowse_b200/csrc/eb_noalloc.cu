@@ -57,7 +57,7 @@ extern "C" int eb_attention_decode_noalloc(const eb_attn_desc* d, const eb_attn_
   if (d->q_stride || d->kv_stride || d->o_stride) return EB_ERR_UNSUPPORTED;
   // The split-K plan for this shape must fit the fixed scratch; refuse, before
   // touching the device, a shape whose partials would not.
-  const size_t need = eb_attention_decode_workspace_bytes(d, 1, pos);
+  const size_t need = decode_plan_bytes(d, 1, pos);
   if (need > (size_t)EB_NOALLOC_SCRATCH_BYTES) return EB_ERR_WORKSPACE;
   int major = 0, dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||

@@ -217,7 +217,8 @@ EB_API int eb_attention_decode_batched(const eb_attn_desc* desc, const eb_attn_l
                                 void* workspace, size_t workspace_bytes, eb_stream_t stream);
 
 /* Workspace for eb_attention_decode(_batched) with contexts up to max_pos+1
- * rows. 0 means the call needs none. */
+ * rows: one workspace of this size serves every call with pos (or the
+ * batched max_pos) <= max_pos. 0 means no such call needs one. */
 EB_API size_t eb_attention_decode_workspace_bytes(const eb_attn_desc* desc, int64_t batch,
                                            int64_t max_pos);
 
@@ -236,10 +237,10 @@ EB_API int eb_workspace_init(void* workspace, size_t workspace_bytes, eb_stream_
  * serving loop that must never call into an allocator between steps. No
  * counterpart in the reference (its kernels need no scratch).
  * The split-K scratch is a fixed EB_NOALLOC_SCRATCH_BYTES array inside this
- * library, held by every GPU that loads it until the process exits. A shape
- * whose split-K plan needs more (eb_attention_decode_workspace_bytes(desc, 1,
- * pos) > EB_NOALLOC_SCRATCH_BYTES) is refused with EB_ERR_WORKSPACE before
- * any device work. The call allocates nothing; its first call on a device
+ * library, held by every GPU that loads it until the process exits. A call
+ * whose split-K plan at pos needs more is refused with EB_ERR_WORKSPACE before
+ * any device work (never one with eb_attention_decode_workspace_bytes(desc,
+ * 1, pos) <= EB_NOALLOC_SCRATCH_BYTES). The call allocates nothing; its first call on a device
  * looks up the array's device address (cudaGetSymbolAddress), so make that
  * first call before any stream capture. All calls on a device share the one
  * array: calls that overlap on the GPU (other streams, other threads) race

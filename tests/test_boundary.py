@@ -77,6 +77,12 @@ def test_workspace_sizes(eb):
     b = eb.attention_decode_workspace_bytes(d, 64, 32767)
     assert a > 0 and b > a and a % 256 == 0
     assert eb.attention_decode_workspace_bytes(d, 1, 10) == 0  # short context: one CTA per head
+    # one workspace sized at max_pos serves every shorter context: the size
+    # never shrinks as max_pos grows (the split-K chunk count itself can)
+    for desc, batch in ((d, 1), (eb.make_desc(32, 8, 64, 1 << 17, dtype_cache=eb.EB_F16), 2),
+                        (eb.make_desc(8, 1, 256, 1 << 17), 1)):
+        sizes = [eb.attention_decode_workspace_bytes(desc, batch, p) for p in range(0, 20000, 7)]
+        assert all(x <= y for x, y in zip(sizes, sizes[1:]))
     # f16 hi/lo planes of k and v, then of the prepared q rows
     assert eb.attn_prefill_workspace_bytes(16, 8, 128, 128) == (4 * 128 * 8 + 2 * 128 * 16) * 128 * 2
     assert eb.attn_prefill_workspace_bytes(2, 1, 5, 8) == 0  # SIMT path
