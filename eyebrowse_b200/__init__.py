@@ -52,7 +52,8 @@ class AttnDesc(ctypes.Structure):
                 ("dtype_qkv", ctypes.c_int32), ("dtype_cache", ctypes.c_int32),
                 ("dtype_out", ctypes.c_int32), ("q_stride", ctypes.c_int32),
                 ("kv_stride", ctypes.c_int32), ("o_stride", ctypes.c_int32),
-                ("eps", ctypes.c_float), ("scale", ctypes.c_float)]
+                ("eps", ctypes.c_float), ("scale", ctypes.c_float),
+                ("window", ctypes.c_int32)]
 
 
 class AttnLayer(ctypes.Structure):
@@ -195,11 +196,15 @@ def rope_tables(max_seq: int, head_dim: int, theta: float, rope_angles: int | No
 
 # ---------------------------------------------------------------- fused primitive
 def make_desc(n_heads, n_kv_heads, head_dim, max_seq, *, dtype_qkv=EB_F32, dtype_cache=EB_F32,
-              dtype_out=EB_F32, eps=1e-6, scale=None, q_stride=0, kv_stride=0, o_stride=0):
+              dtype_out=EB_F32, eps=1e-6, scale=None, q_stride=0, kv_stride=0, o_stride=0,
+              window=0):
+    """eb_attn_desc. window > 0 restricts each query row i to key rows
+    i - window < j <= i (sliding-window layers); 0 attends the whole causal
+    context."""
     if scale is None:
         scale = head_dim ** -0.5
     return AttnDesc(n_heads, n_kv_heads, head_dim, max_seq, dtype_qkv, dtype_cache, dtype_out,
-                    q_stride, kv_stride, o_stride, eps, scale)
+                    q_stride, kv_stride, o_stride, eps, scale, window)
 
 
 def make_layer(q_norm_w=None, k_norm_w=None, v_norm_w=None, rope_cos=None, rope_sin=None):

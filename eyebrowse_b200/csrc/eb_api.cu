@@ -134,7 +134,13 @@ static bool desc_ok(const eb_attn_desc* d) {
   if (d->max_seq <= 0) return false;
   if (!dtype_ok(d->dtype_qkv) || !dtype_ok(d->dtype_cache) || !dtype_ok(d->dtype_out)) return false;
   if (d->q_stride < 0 || d->kv_stride < 0 || d->o_stride < 0) return false;
+  if (d->window < 0) return false;
   return true;
+}
+// A decode call at max_pos attends at most this many rows minus one: a
+// sliding window caps the context the split-K plan covers.
+static int64_t attended_max_pos(const eb_attn_desc* d, int64_t max_pos) {
+  return d->window > 0 ? std::min<int64_t>(max_pos, (int64_t)d->window - 1) : max_pos;
 }
 static int64_t qs_of(const eb_attn_desc* d) {
   return d->q_stride ? d->q_stride : (int64_t)d->n_heads * d->head_dim;
@@ -147,7 +153,8 @@ static int64_t os_of(const eb_attn_desc* d) {
 }
 
 size_t decode_plan_bytes(const eb_attn_desc* d, int64_t batch, int64_t max_pos) {
-  return plan_decode(batch, d->n_heads, d->n_kv_heads, d->head_dim, d->dtype_cache, max_pos)
+  return plan_decode(batch, d->n_heads, d->n_kv_heads, d->head_dim, d->dtype_cache,
+                     attended_max_pos(d, max_pos))
       .bytes;
 }
 
@@ -161,11 +168,12 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
   const float* cos_t = L ? L->rope_cos : nullptr;
   const float* sin_t = L ? L->rope_sin : nullptr;
   if ((cos_t == nullptr) != (sin_t == nullptr)) return EB_ERR_INVALID_ARGUMENT;
-  DecodePlan p = plan_decode(batch, d->n_heads, d->n_kv_heads, hd, d->dtype_cache, max_pos);
+  const int64_t span_pos = attended_max_pos(d, max_pos);
+  DecodePlan p = plan_decode(batch, d->n_heads, d->n_kv_heads, hd, d->dtype_cache, span_pos);
   const bool vec = (hd == 64 || hd == 128 || hd == 256);
   if (vec && p.cmax > 1 && (ws == nullptr || ws_bytes < p.bytes)) {
     if (ws != nullptr && ws_bytes != 0) return EB_ERR_WORKSPACE;
-    p.chunk = (int)(max_pos + 1);  // no workspace: one CTA walks the whole context
+    p.chunk = (int)(span_pos + 1);  // no workspace: one CTA walks the whole context
     p.cmax = 1;
   }
   if (vec) {
@@ -193,6 +201,7 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
     a.sin_t = sin_t;
     a.positions = positions;
     a.pos_scalar = (int)pos_scalar;
+    a.window = d->window;
     a.H = d->n_heads;
     a.Hkv = d->n_kv_heads;
     a.hd = hd;
@@ -255,6 +264,7 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
   s.Hkv = d->n_kv_heads;
   s.hd = hd;
   s.qpos0 = (int)pos_scalar;
+  s.window = d->window;
   s.positions = positions;
   s.q_norm_w = L ? L->q_norm_w : nullptr;
   s.cos_t = cos_t;
@@ -576,6 +586,7 @@ static int prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, int64_t
     a.S = (int)seq;
     a.H = d->n_heads;
     a.Hkv = d->n_kv_heads;
+    a.window = d->window;
     a.scale_log2 = d->scale * kLog2e;
     a.err = error_word_ptr();
     if (!a.err) return EB_ERR_CUDA;
@@ -598,6 +609,7 @@ static int prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, int64_t
   s.H = d->n_heads;
   s.Hkv = d->n_kv_heads;
   s.hd = hd;
+  s.window = d->window;
   s.q_norm_w = L ? L->q_norm_w : nullptr;
   s.cos_t = cos_t;
   s.sin_t = sin_t;
@@ -655,7 +667,7 @@ size_t eb_attention_decode_workspace_bytes(const eb_attn_desc* d, int64_t batch,
                                            int64_t max_pos) {
   if (!desc_ok(d) || batch <= 0 || max_pos < 0) return 0;
   return decode_workspace_bound(batch, d->n_heads, d->n_kv_heads, d->head_dim, d->dtype_cache,
-                                max_pos);
+                                attended_max_pos(d, max_pos));
 }
 
 int eb_attention_decode(const eb_attn_desc* d, const eb_attn_layer* L, int64_t pos,

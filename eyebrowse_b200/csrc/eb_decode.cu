@@ -75,7 +75,9 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
   const int b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pos = a.positions ? a.positions[b] : a.pos_scalar;
-  const int n_rows = pos + 1;
+  // rows [row_lo, pos]: the whole context, or the last `window` rows of it
+  const int row_lo = a.window > 0 ? max(0, pos - a.window + 1) : 0;
+  const int n_rows = pos + 1 - row_lo;
   const int n_chunks = (n_rows + a.chunk - 1) / a.chunk;
   if (c >= n_chunks) return;
   const int head0 = kvh * (G * gsubs) + sub * G;  // first query head of this CTA
@@ -129,8 +131,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
     for (int e = 0; e < EPL; e++) acc[g][e] = 0.f;
   }
 
-  const int row_begin = c * a.chunk;
-  const int row_end = min(row_begin + a.chunk, n_rows);
+  const int row_begin = row_lo + c * a.chunk;
+  const int row_end = min(row_begin + a.chunk, pos + 1);
   const int64_t rstride = (int64_t)a.Hkv * HD;
   const TC* kc = reinterpret_cast<const TC*>(a.kcache) + (int64_t)b * a.cache_bstride +
                  (int64_t)kvh * HD + sl * VEC;

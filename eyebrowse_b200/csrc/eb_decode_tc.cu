@@ -58,11 +58,13 @@ __global__ void __launch_bounds__(96)
   const int kvh = grp / gsubs, sub = grp % gsubs;
   const int head0 = kvh * (G * gsubs) + sub * G;
   const int pos = a.positions ? a.positions[b] : a.pos_scalar;
-  const int n_rows = pos + 1;
+  // rows [row_lo, pos]: the whole context, or the last `window` rows of it
+  const int row_lo = a.window > 0 ? max(0, pos - a.window + 1) : 0;
+  const int n_rows = pos + 1 - row_lo;
   const int n_chunks = (n_rows + a.chunk - 1) / a.chunk;
   if (c >= n_chunks) return;
-  const int row_begin = c * a.chunk;
-  const int row_end = min(row_begin + a.chunk, n_rows);
+  const int row_begin = row_lo + c * a.chunk;
+  const int row_end = min(row_begin + a.chunk, pos + 1);
   const int n_tiles = (row_end - row_begin + BN - 1) / BN;
   const bool last_chunk = c == n_chunks - 1;
 

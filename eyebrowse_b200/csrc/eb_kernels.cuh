@@ -71,6 +71,7 @@ struct SimtArgs {
   int64_t o_stride, o_bstride;
   int rows, H, Hkv, hd;
   int qpos0;
+  int window;  // > 0: sliding window (keys pos - window < j <= pos)
   const int32_t* positions;
   const float* q_norm_w;
   const float* cos_t;
@@ -98,6 +99,7 @@ struct DecodeArgs {
   const float* sin_t;
   const int32_t* positions;  // device, per sequence; nullptr -> pos_scalar
   int pos_scalar;
+  int window;          // > 0: rows pos - window < j <= pos only
   int H, Hkv, hd, chunk, cmax;
   int max_seq;         // cache rows per sequence (tensor-map extent)
   float eps, scale_log2;
@@ -129,6 +131,7 @@ struct PrefillArgs {
   int dtype_o;
   int64_t o_stride;  // elements between output rows
   int S, H, Hkv;
+  int window;  // > 0: key j is visible to query row i iff i - window < j <= i
   float scale_log2;
   unsigned* err;
   // Head gather (n_dst > 0): o is unused; head h of row i goes to row i,

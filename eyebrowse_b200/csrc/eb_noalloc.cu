@@ -51,7 +51,7 @@ extern "C" int eb_attention_decode_noalloc(const eb_attn_desc* d, const eb_attn_
                                            eb_stream_t stream) {
   if (!d || d->n_heads <= 0 || d->n_kv_heads <= 0 || d->n_heads % d->n_kv_heads ||
       d->head_dim <= 0 || d->head_dim > 256 || (d->head_dim & 1) || d->max_seq <= 0 || pos < 0 ||
-      pos >= d->max_seq)
+      pos >= d->max_seq || d->window < 0)
     return EB_ERR_INVALID_ARGUMENT;
   if (!q || !k || !v || !kcache || !vcache || !o) return EB_ERR_INVALID_ARGUMENT;
   if (d->q_stride || d->kv_stride || d->o_stride) return EB_ERR_UNSUPPORTED;

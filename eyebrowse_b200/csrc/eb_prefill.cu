@@ -30,6 +30,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <climits>
 #include <cstring>
 #include <mutex>
 
@@ -105,7 +106,10 @@ __device__ __forceinline__ bool named_bar_and(int id, int n, bool v) {
 
 
 
-template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV>
+// WIN: a sliding window narrower than the sequence (a.window). Its own
+// instantiation, so the plain causal kernel carries none of the window's
+// index arithmetic.
+template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV, bool WIN>
 __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                       const __grid_constant__ CUtensorMap tmQlo,
@@ -145,7 +149,10 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
   const int kvh = (grp * NQ) / (a.H / a.Hkv);
   const int q0 = qt * 128;
   const int kv_rows = min(q0 + 128, a.S);
-  const int n_tiles = (kv_rows + BN - 1) / BN;
+  // With a sliding window the tile loop starts at the first key tile that
+  // any row of this query tile sees; tile j of the loop is key tile j0 + j.
+  const int j0 = WIN ? max(0, q0 - a.window + 1) / BN : 0;
+  const int n_tiles = (kv_rows + BN - 1) / BN - j0;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(kBarQ), 1);
@@ -208,8 +215,9 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         mbar_arrive_expect_tx(kf, C::K_BYTES);
 #pragma unroll
         for (int hb = 0; hb < C::HB; hb++) {
-          tma_load_3d(kst + hb * C::KV_BOX, &tmK, kf, hb * 64, kvh, j * BN);
-          if (SPLIT) tma_load_3d(kst + (C::HB + hb) * C::KV_BOX, &tmKlo, kf, hb * 64, kvh, j * BN);
+          tma_load_3d(kst + hb * C::KV_BOX, &tmK, kf, hb * 64, kvh, (j0 + j) * BN);
+          if (SPLIT)
+            tma_load_3d(kst + (C::HB + hb) * C::KV_BOX, &tmKlo, kf, hb * 64, kvh, (j0 + j) * BN);
         }
         kiss[sk]++;
         if (j >= NSTV && !mbar_wait(bar(kVEmpty0 + sv), (j / NSTV - 1) & 1, abort_flag, a.err,
@@ -219,8 +227,9 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         mbar_arrive_expect_tx(vf, C::K_BYTES);
 #pragma unroll
         for (int hb = 0; hb < C::HB; hb++) {
-          tma_load_3d(vst + hb * C::KV_BOX, &tmV, vf, hb * 64, kvh, j * BN);
-          if (SPLIT) tma_load_3d(vst + (C::HB + hb) * C::KV_BOX, &tmVlo, vf, hb * 64, kvh, j * BN);
+          tma_load_3d(vst + hb * C::KV_BOX, &tmV, vf, hb * 64, kvh, (j0 + j) * BN);
+          if (SPLIT)
+            tma_load_3d(vst + (C::HB + hb) * C::KV_BOX, &tmVlo, vf, hb * 64, kvh, (j0 + j) * BN);
         }
         viss[sv]++;
       }
@@ -374,7 +383,12 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const float sl2 = a.scale_log2;
     const uint32_t tO = tmem + lane_off + t * HD;
-    float m_run = -INFINITY, l_run = 0.f;
+    // With a window the running max starts finite: a row can see no key of
+    // its first tiles (S row all -inf), and -inf - (-inf) would turn its P
+    // into NaN. Any finite score later rescales by ex2(-1e30 - m) = 0.
+    float m_run = WIN ? -1e30f : -INFINITY, l_run = 0.f;
+    // lowest visible key of this row (none below it with no window)
+    const int k_lo = WIN ? q_row - a.window + 1 : INT_MIN;
     bool ok = true;
     for (int j = 0; j < n_tiles; j++) {
       const int b = j % NSB;
@@ -387,8 +401,9 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         break;
       }
       tc_fence_after();
-      const int k0 = j * BN;
-      const bool diag = k0 + BN - 1 > q_row;  // tile crosses the causal diagonal
+      const int k0 = (j0 + j) * BN;
+      // the tile crosses the causal diagonal or the window's lower edge
+      const bool diag = k0 + BN - 1 > q_row || (WIN && k0 < k_lo);
       // pass 1: the row max (the S row is the only live data here). The first
       // (up to) 64 columns stay in registers for pass 2, which re-reads only
       // the rest from TMEM.
@@ -409,7 +424,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         if (diag) {
 #pragma unroll
           for (int c = 0; c < BN; c++)
-            if (k0 + c > q_row) x[c] = -INFINITY;
+            if (k0 + c > q_row || (WIN && k0 + c < k_lo)) x[c] = -INFINITY;
         }
         // 8 independent chains, then a short tree
         float mc[8];
@@ -477,7 +492,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
           if (diag) {
 #pragma unroll
             for (int c = 0; c < HALF; c++)
-              if (k0 + hbase + c > q_row) x[c] = -INFINITY;
+              if (k0 + hbase + c > q_row || (WIN && k0 + hbase + c < k_lo)) x[c] = -INFINITY;
           }
         }
         uint32_t ph[HALF / 2];
@@ -693,12 +708,12 @@ static bool make_out_map(CUtensorMap* m, uint64_t base, int S, int64_t h_total, 
   return r == CUDA_SUCCESS;
 }
 
-template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV>
-static cudaError_t run_prefill(const PrefillArgs& a, const void* q16, const void* k16,
-                               const void* v16, const void* split, const GatherSpec* g,
-                               cudaStream_t st) {
+template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV, bool WIN>
+static cudaError_t run_prefill_k(const PrefillArgs& a, const void* q16, const void* k16,
+                                 const void* v16, const void* split, const GatherSpec* g,
+                                 cudaStream_t st) {
   using C = PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>;
-  auto kern = prefill_tc_kernel<HD, BN, NQ, SPLIT, BF16, NSTK, NSTV>;
+  auto kern = prefill_tc_kernel<HD, BN, NQ, SPLIT, BF16, NSTK, NSTV, WIN>;
   static unsigned configured = 0;  // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -749,6 +764,18 @@ static cudaError_t run_prefill(const PrefillArgs& a, const void* q16, const void
   kern<<<(unsigned)(n_qt * (a.H / NQ)), C::THREADS, C::SMEM, st>>>(mq, mql, mk, mv, mkl, mvl, gm,
                                                                      ka);
   return cudaGetLastError();
+}
+
+// A window of at least S rows masks nothing: the causal kernel serves it.
+template <int HD, int BN, int NQ, bool SPLIT, bool BF16, int NSTK, int NSTV>
+static cudaError_t run_prefill(const PrefillArgs& a, const void* q16, const void* k16,
+                               const void* v16, const void* split, const GatherSpec* g,
+                               cudaStream_t st) {
+  return (a.window > 0 && a.window < a.S)
+             ? run_prefill_k<HD, BN, NQ, SPLIT, BF16, NSTK, NSTV, true>(a, q16, k16, v16, split,
+                                                                        g, st)
+             : run_prefill_k<HD, BN, NQ, SPLIT, BF16, NSTK, NSTV, false>(a, q16, k16, v16, split,
+                                                                         g, st);
 }
 
 bool prefill_tc_supported(int hd) { return hd == 64 || hd == 128 || hd == 256; }

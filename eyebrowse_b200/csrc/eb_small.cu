@@ -442,7 +442,8 @@ __global__ void __launch_bounds__(kSimtWarps * 32) attn_simt_kernel(SimtArgs a) 
   }
   float m = -INFINITY, l = 0.f;
   const int64_t kbase = b * a.kv_bstride + (int64_t)kvh * hd;
-  for (int j = 0; j <= pos; j++) {
+  const int j_lo = a.window > 0 ? max(0, pos - a.window + 1) : 0;
+  for (int j = j_lo; j <= pos; j++) {
     const int64_t ko = kbase + (int64_t)j * a.kv_stride;
     float s = 0.f;
 #pragma unroll

@@ -232,6 +232,9 @@ struct Attention {
   size_t n_heads = 0, n_kv_heads = 0, head_dim = 0;
   float scale = 0.f, eps = 1e-6f;
   DType dtype_qkv = DType::F32, dtype_out = DType::F32;
+  // Sliding-window layers (Gemma local attention; the reference defers them):
+  // row i sees keys i - window < j <= i. 0 = the whole causal context.
+  size_t window = 0;
 
   eb_attn_desc desc(const KvCache& kv) const {
     eb_attn_desc d{};
@@ -244,6 +247,7 @@ struct Attention {
     d.dtype_out = (int32_t)dtype_out;
     d.eps = eps;
     d.scale = scale;
+    d.window = (int32_t)window;
     return d;
   }
   eb_attn_layer layer(const Rope& rope) const {

@@ -122,6 +122,8 @@ typedef struct {
   int32_t o_stride;    /* elements between consecutive rows of o; 0 = n_heads*head_dim */
   float eps;           /* RMSNorm epsilon (Config rms_eps) */
   float scale;         /* softmax scale (1/sqrt(head_dim), or 1.0 for Gemma 4) */
+  int32_t window;      /* sliding window (Gemma local layers): query row i sees key rows
+                          j with i - window < j <= i; 0 = the whole causal context */
 } eb_attn_desc;
 
 /* Optional per-layer inputs; any NULL pointer disables that step. */

@@ -194,26 +194,42 @@ static void attn_row(const float* qrow, const float* k, const float* v, float* o
   }
 }
 
-void orc_attn_prefill(const float* q, const float* k, const float* v, float* o,
-                      size_t h, size_t hkv, size_t s, size_t hd, float scale) {
-  /* crates/eyebrowse-kernels/src/testutil.rs:130-172 */
+/* First key row that query row i sees. window 0: every row j <= i (the
+ * reference's causal mask). window > 0: i - window < j <= i, the sliding-window
+ * mask of HF transformers (masking_utils.sliding_window_causal_mask_function:
+ * kv_idx > q_idx - sliding_window, and causal); the reference lists sliding
+ * windows as not yet supported (README.md:25). */
+static size_t window_lo(size_t i, size_t window) {
+  return (window && i + 1 > window) ? i + 1 - window : 0;
+}
+
+void orc_attn_prefill_window(const float* q, const float* k, const float* v, float* o,
+                             size_t h, size_t hkv, size_t s, size_t hd, float scale,
+                             size_t window) {
+  /* crates/eyebrowse-kernels/src/testutil.rs:130-172, keys from window_lo(i) */
   size_t group = h / hkv;
   float* scores = (float*)malloc(sizeof(float) * (s ? s : 1));
   for (size_t i = 0; i < s; i++) {
+    size_t lo = window_lo(i, window);
     for (size_t hh = 0; hh < h; hh++) {
       size_t kvh = hh / group;
       size_t qbase = (i * h + hh) * hd;
-      attn_row(q + qbase, k + kvh * hd, v + kvh * hd, o + qbase, i + 1, hkv * hd, hd, scale,
-               scores);
+      attn_row(q + qbase, k + (lo * hkv + kvh) * hd, v + (lo * hkv + kvh) * hd, o + qbase,
+               i + 1 - lo, hkv * hd, hd, scale, scores);
     }
   }
   free(scores);
 }
 
+void orc_attn_prefill(const float* q, const float* k, const float* v, float* o,
+                      size_t h, size_t hkv, size_t s, size_t hd, float scale) {
+  orc_attn_prefill_window(q, k, v, o, h, hkv, s, hd, scale, 0);
+}
+
 typedef struct {
   const float *q, *k, *v;
   float* o;
-  size_t h, hkv, s, hd, row_begin, row_end, head_begin, head_end;
+  size_t h, hkv, s, hd, row_begin, row_end, head_begin, head_end, window;
   float scale;
   atomic_size_t next;
 } prefill_job;
@@ -227,10 +243,12 @@ static void* prefill_worker(void* arg) {
     size_t t = atomic_fetch_add(&jb->next, 1);
     if (t >= jb->row_end - jb->row_begin) break;
     size_t i = jb->row_end - 1 - t;
+    size_t lo = window_lo(i, jb->window);
     for (size_t hh = jb->head_begin; hh < jb->head_end; hh++) {
       size_t kvh = hh / group;
       size_t qbase = (i * jb->h + hh) * jb->hd;
-      attn_row(jb->q + qbase, jb->k + kvh * jb->hd, jb->v + kvh * jb->hd, jb->o + qbase, i + 1,
+      size_t kbase = (lo * jb->hkv + kvh) * jb->hd;
+      attn_row(jb->q + qbase, jb->k + kbase, jb->v + kbase, jb->o + qbase, i + 1 - lo,
                jb->hkv * jb->hd, jb->hd, jb->scale, scores);
     }
   }
@@ -241,10 +259,10 @@ static void* prefill_worker(void* arg) {
 void orc_attn_prefill_part(const float* q, const float* k, const float* v, float* o,
                            size_t h, size_t hkv, size_t s, size_t hd, float scale,
                            size_t row_begin, size_t row_end, size_t head_begin,
-                           size_t head_end, int nthreads) {
+                           size_t head_end, int nthreads, size_t window) {
   prefill_job jb;
   jb.q = q; jb.k = k; jb.v = v; jb.o = o;
-  jb.h = h; jb.hkv = hkv; jb.s = s; jb.hd = hd;
+  jb.h = h; jb.hkv = hkv; jb.s = s; jb.hd = hd; jb.window = window;
   jb.row_begin = row_begin; jb.row_end = row_end;
   jb.head_begin = head_begin; jb.head_end = head_end;
   jb.scale = scale;
@@ -257,26 +275,34 @@ void orc_attn_prefill_part(const float* q, const float* k, const float* v, float
   free(th);
 }
 
-void orc_attn_decode(const float* q, const float* kc, const float* vc, float* o,
-                     size_t h, size_t hkv, size_t pos, size_t hd, size_t max_seq, float scale) {
-  /* crates/eyebrowse-kernels/src/testutil.rs:177-218 */
+void orc_attn_decode_window(const float* q, const float* kc, const float* vc, float* o,
+                            size_t h, size_t hkv, size_t pos, size_t hd, size_t max_seq,
+                            float scale, size_t window) {
+  /* crates/eyebrowse-kernels/src/testutil.rs:177-218, cache rows from window_lo(pos) */
   (void)max_seq;
   size_t group = h / hkv;
+  size_t lo = window_lo(pos, window);
   float* scores = (float*)malloc(sizeof(float) * (pos + 1));
   for (size_t hh = 0; hh < h; hh++) {
     size_t kvh = hh / group;
     size_t qbase = hh * hd;
-    attn_row(q + qbase, kc + kvh * hd, vc + kvh * hd, o + qbase, pos + 1, hkv * hd, hd, scale,
+    size_t kbase = (lo * hkv + kvh) * hd;
+    attn_row(q + qbase, kc + kbase, vc + kbase, o + qbase, pos + 1 - lo, hkv * hd, hd, scale,
              scores);
   }
   free(scores);
+}
+
+void orc_attn_decode(const float* q, const float* kc, const float* vc, float* o,
+                     size_t h, size_t hkv, size_t pos, size_t hd, size_t max_seq, float scale) {
+  orc_attn_decode_window(q, kc, vc, o, h, hkv, pos, hd, max_seq, scale, 0);
 }
 
 typedef struct {
   const float *q, *kc, *vc;
   float* o;
   const int32_t* pos;
-  size_t batch, h, hkv, hd, max_seq, cache_stride;
+  size_t batch, h, hkv, hd, max_seq, cache_stride, window;
   float scale;
   atomic_size_t next;
 } decode_job;
@@ -291,10 +317,10 @@ static void* decode_worker(void* arg) {
     size_t b = t / jb->h, hh = t % jb->h;
     size_t kvh = hh / group;
     size_t qbase = (b * jb->h + hh) * jb->hd;
-    const float* kb = jb->kc + b * jb->cache_stride;
-    const float* vb = jb->vc + b * jb->cache_stride;
-    attn_row(jb->q + qbase, kb + kvh * jb->hd, vb + kvh * jb->hd, jb->o + qbase,
-             (size_t)jb->pos[b] + 1, jb->hkv * jb->hd, jb->hd, jb->scale, scores);
+    const size_t lo = window_lo((size_t)jb->pos[b], jb->window);
+    const size_t kbase = b * jb->cache_stride + (lo * jb->hkv + kvh) * jb->hd;
+    attn_row(jb->q + qbase, jb->kc + kbase, jb->vc + kbase, jb->o + qbase,
+             (size_t)jb->pos[b] + 1 - lo, jb->hkv * jb->hd, jb->hd, jb->scale, scores);
   }
   free(scores);
   return NULL;
@@ -303,8 +329,9 @@ static void* decode_worker(void* arg) {
 void orc_attn_decode_batched(const float* q, const float* kc, const float* vc, float* o,
                              size_t batch, const int32_t* pos, size_t h, size_t hkv,
                              size_t hd, size_t max_seq, size_t cache_stride, float scale,
-                             int nthreads) {
+                             int nthreads, size_t window) {
   decode_job jb;
+  jb.window = window;
   jb.q = q; jb.kc = kc; jb.vc = vc; jb.o = o; jb.pos = pos;
   jb.batch = batch; jb.h = h; jb.hkv = hkv; jb.hd = hd; jb.max_seq = max_seq;
   jb.cache_stride = cache_stride; jb.scale = scale;
@@ -328,7 +355,7 @@ void orc_attention_prefill(const float* q, const float* k, const float* v,
                            float eps, const float* cos_t, const float* sin_t,
                            float* kcache, float* vcache, float* o,
                            size_t seq, size_t h, size_t hkv, size_t hd, size_t max_seq,
-                           float scale, int cache_round, int q_round) {
+                           float scale, int cache_round, int q_round, size_t window) {
   /* crates/eyebrowse-nn/src/attention.rs:49-117, after the projections (:58-60) */
   float* qn = dup(q, seq * h * hd);
   float* kn = dup(k, seq * hkv * hd);
@@ -345,7 +372,7 @@ void orc_attention_prefill(const float* q, const float* k, const float* v,
   round_as(qn, seq * h * hd, q_round);
   orc_kv_write(kcache, kn, hkv, seq, hd, max_seq, 0); /* :78-87 */
   orc_kv_write(vcache, vn, hkv, seq, hd, max_seq, 0); /* :88-97 */
-  orc_attn_prefill(qn, kn, vn, o, h, hkv, seq, hd, scale); /* :104-115 */
+  orc_attn_prefill_window(qn, kn, vn, o, h, hkv, seq, hd, scale, window); /* :104-115 */
   free(qn); free(kn); free(vn);
 }
 
@@ -354,7 +381,7 @@ void orc_attention_decode(const float* q, const float* k, const float* v,
                           float eps, const float* cos_t, const float* sin_t,
                           float* kcache, float* vcache, float* o,
                           size_t pos, size_t h, size_t hkv, size_t hd, size_t max_seq,
-                          float scale, int cache_round) {
+                          float scale, int cache_round, size_t window) {
   /* crates/eyebrowse-nn/src/attention.rs:120-185, after the projections (:129-131) */
   float* qn = dup(q, h * hd);
   float* kn = dup(k, hkv * hd);
@@ -370,6 +397,7 @@ void orc_attention_decode(const float* q, const float* k, const float* v,
   round_as(vn, hkv * hd, cache_round);
   orc_kv_write(kcache, kn, hkv, 1, hd, max_seq, pos); /* :149-168 */
   orc_kv_write(vcache, vn, hkv, 1, hd, max_seq, pos);
-  orc_attn_decode(qn, kcache, vcache, o, h, hkv, pos, hd, max_seq, scale); /* :171-183 */
+  orc_attn_decode_window(qn, kcache, vcache, o, h, hkv, pos, hd, max_seq, scale,
+                         window); /* :171-183 */
   free(qn); free(kn); free(vn);
 }

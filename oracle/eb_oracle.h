@@ -69,18 +69,31 @@ void orc_kv_write(float* cache, const float* src, size_t hkv, size_t count, size
 void orc_attn_prefill(const float* q, const float* k, const float* v, float* o,
                       size_t h, size_t hkv, size_t s, size_t hd, float scale);
 
+/* orc_attn_prefill with a sliding window: row i attends key rows j with
+ * i - window < j <= i (HF transformers' sliding-window causal mask; no
+ * counterpart in the reference, which defers sliding windows). window 0 is
+ * orc_attn_prefill. */
+void orc_attn_prefill_window(const float* q, const float* k, const float* v, float* o,
+                             size_t h, size_t hkv, size_t s, size_t hd, float scale,
+                             size_t window);
+
 /* Same computation restricted to query rows [row_begin,row_end) and query heads
  * [head_begin,head_end), spread over `nthreads` POSIX threads (parallel over
  * (row, head) with the identical inner loop). Used by the timed CPU baseline. */
 void orc_attn_prefill_part(const float* q, const float* k, const float* v, float* o,
                            size_t h, size_t hkv, size_t s, size_t hd, float scale,
                            size_t row_begin, size_t row_end, size_t head_begin,
-                           size_t head_end, int nthreads);
+                           size_t head_end, int nthreads, size_t window);
 
 /* Single decode step: q [h,hd] attends rows 0..=pos of caches [max_seq,hkv,hd].
  * crates/eyebrowse-kernels/src/testutil.rs:177-218. */
 void orc_attn_decode(const float* q, const float* kc, const float* vc, float* o,
                      size_t h, size_t hkv, size_t pos, size_t hd, size_t max_seq, float scale);
+
+/* orc_attn_decode over cache rows pos - window < j <= pos (window 0: all). */
+void orc_attn_decode_window(const float* q, const float* kc, const float* vc, float* o,
+                            size_t h, size_t hkv, size_t pos, size_t hd, size_t max_seq,
+                            float scale, size_t window);
 
 /* Batched decode baseline: `batch` independent decode steps, sequence b using
  * q + b*h*hd, caches + b*cache_stride, position pos[b]; parallel over
@@ -88,7 +101,7 @@ void orc_attn_decode(const float* q, const float* kc, const float* vc, float* o,
 void orc_attn_decode_batched(const float* q, const float* kc, const float* vc, float* o,
                              size_t batch, const int32_t* pos, size_t h, size_t hkv,
                              size_t hd, size_t max_seq, size_t cache_stride, float scale,
-                             int nthreads);
+                             int nthreads, size_t window);
 
 /* Storage-rounding model for the composite functions below (no reference
  * counterpart: the reference stores f32 only). 0 = f32, 1 = f16, 2 = bf16. */
@@ -97,7 +110,8 @@ enum { ORC_F32 = 0, ORC_F16 = 1, ORC_BF16 = 2 };
 /* The attention part of Attention::prefill (crates/eyebrowse-nn/src/attention.rs:49-117)
  * from the projection outputs on: q/k/v RMSNorm when a weight is given (:62-74),
  * RoPE at base 0 (:75-76), kv_write of post-RoPE k and post-norm v at row 0
- * (:78-97), causal attention over the fresh k/v (:104-115).
+ * (:78-97), causal attention over the fresh k/v (:104-115), within `window`
+ * rows when window > 0 (see orc_attn_prefill_window).
  * q [seq,h,hd], k/v [seq,hkv,hd]; caches [max_seq,hkv,hd]; o [seq,h,hd].
  * cos/sin NULL skips RoPE. cache_round rounds the stored k/v (and the k/v the
  * attention reads, which equal the stored rows); q_round rounds the post-RoPE q
@@ -107,7 +121,7 @@ void orc_attention_prefill(const float* q, const float* k, const float* v,
                            float eps, const float* cos_t, const float* sin_t,
                            float* kcache, float* vcache, float* o,
                            size_t seq, size_t h, size_t hkv, size_t hd, size_t max_seq,
-                           float scale, int cache_round, int q_round);
+                           float scale, int cache_round, int q_round, size_t window);
 
 /* The attention part of Attention::decode (crates/eyebrowse-nn/src/attention.rs:120-185):
  * norms (:133-144), RoPE at base_pos = pos (:146-147), kv_write at row pos
@@ -118,7 +132,7 @@ void orc_attention_decode(const float* q, const float* k, const float* v,
                           float eps, const float* cos_t, const float* sin_t,
                           float* kcache, float* vcache, float* o,
                           size_t pos, size_t h, size_t hkv, size_t hd, size_t max_seq,
-                          float scale, int cache_round);
+                          float scale, int cache_round, size_t window);
 
 #ifdef __cplusplus
 }

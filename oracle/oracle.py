@@ -51,19 +51,24 @@ def lib():
         L.orc_rope_tables.argtypes = [_fp, _fp, _sz, _sz, _sz, ctypes.c_float]
         L.orc_kv_write.argtypes = [_fp, _fp, _sz, _sz, _sz, _sz, _sz]
         L.orc_attn_prefill.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz, ctypes.c_float]
+        L.orc_attn_prefill_window.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz,
+                                              ctypes.c_float, _sz]
         L.orc_attn_prefill_part.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz,
-                                            ctypes.c_float, _sz, _sz, _sz, _sz, ctypes.c_int]
+                                            ctypes.c_float, _sz, _sz, _sz, _sz, ctypes.c_int,
+                                            _sz]
         L.orc_attn_decode.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz, _sz,
                                       ctypes.c_float]
+        L.orc_attn_decode_window.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz, _sz,
+                                             ctypes.c_float, _sz]
         L.orc_attn_decode_batched.argtypes = [_fp, _fp, _fp, _fp, _sz,
                                               ctypes.POINTER(ctypes.c_int32), _sz, _sz, _sz,
-                                              _sz, _sz, ctypes.c_float, ctypes.c_int]
+                                              _sz, _sz, ctypes.c_float, ctypes.c_int, _sz]
         L.orc_attention_prefill.argtypes = [_fp, _fp, _fp, _fp, _fp, _fp, ctypes.c_float, _fp,
                                             _fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz, _sz,
-                                            ctypes.c_float, ctypes.c_int, ctypes.c_int]
+                                            ctypes.c_float, ctypes.c_int, ctypes.c_int, _sz]
         L.orc_attention_decode.argtypes = [_fp, _fp, _fp, _fp, _fp, _fp, ctypes.c_float, _fp,
                                            _fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz, _sz,
-                                           ctypes.c_float, ctypes.c_int]
+                                           ctypes.c_float, ctypes.c_int, _sz]
         _lib = L
     return _lib
 
@@ -146,38 +151,52 @@ def kv_write(cache, src, hkv: int, count: int, hd: int, max_seq: int, dst_start:
     return cache
 
 
-def attn_prefill(q, k, v, h: int, hkv: int, s: int, hd: int, scale: float | None = None):
-    """testutil.rs:130-172 (scale defaults to the reference's hard-coded 1/sqrt(hd))."""
+def attn_prefill(q, k, v, h: int, hkv: int, s: int, hd: int, scale: float | None = None,
+                 window: int = 0):
+    """testutil.rs:130-172 (scale defaults to the reference's hard-coded 1/sqrt(hd)).
+    window > 0: row i attends key rows i - window < j <= i (HF's sliding-window
+    causal mask; the reference has no sliding window)."""
     if scale is None:
         scale = 1.0 / np.sqrt(np.float32(hd))
     q, k, v = _f32(q), _f32(k), _f32(v)
     o = np.empty(s * h * hd, np.float32)
-    lib().orc_attn_prefill(_p(q), _p(k), _p(v), _p(o), h, hkv, s, hd, float(scale))
+    if window:
+        lib().orc_attn_prefill_window(_p(q), _p(k), _p(v), _p(o), h, hkv, s, hd, float(scale),
+                                      window)
+    else:
+        lib().orc_attn_prefill(_p(q), _p(k), _p(v), _p(o), h, hkv, s, hd, float(scale))
     return o
 
 
-def attn_prefill_part(q, k, v, h, hkv, s, hd, scale, rows, heads, nthreads: int = 1):
+def attn_prefill_part(q, k, v, h, hkv, s, hd, scale, rows, heads, nthreads: int = 1,
+                      window: int = 0):
     """Rows [rows[0], rows[1]) x heads [heads[0], heads[1]) of attn_prefill, threaded.
     Returns the full-size output buffer (untouched entries are zero)."""
     q, k, v = _f32(q), _f32(k), _f32(v)
     o = np.zeros(s * h * hd, np.float32)
     lib().orc_attn_prefill_part(_p(q), _p(k), _p(v), _p(o), h, hkv, s, hd, float(scale),
-                                rows[0], rows[1], heads[0], heads[1], nthreads)
+                                rows[0], rows[1], heads[0], heads[1], nthreads, window)
     return o
 
 
-def attn_decode(q, kc, vc, h, hkv, pos, hd, max_seq, scale: float | None = None):
-    """testutil.rs:177-218"""
+def attn_decode(q, kc, vc, h, hkv, pos, hd, max_seq, scale: float | None = None,
+                window: int = 0):
+    """testutil.rs:177-218 (window > 0: cache rows pos - window < j <= pos only)"""
     if scale is None:
         scale = 1.0 / np.sqrt(np.float32(hd))
     q, kc, vc = _f32(q), _f32(kc), _f32(vc)
     o = np.empty(h * hd, np.float32)
-    lib().orc_attn_decode(_p(q), _p(kc), _p(vc), _p(o), h, hkv, pos, hd, max_seq, float(scale))
+    if window:
+        lib().orc_attn_decode_window(_p(q), _p(kc), _p(vc), _p(o), h, hkv, pos, hd, max_seq,
+                                     float(scale), window)
+    else:
+        lib().orc_attn_decode(_p(q), _p(kc), _p(vc), _p(o), h, hkv, pos, hd, max_seq,
+                              float(scale))
     return o
 
 
 def attn_decode_batched(q, kc, vc, pos, h, hkv, hd, max_seq, cache_stride, scale,
-                        nthreads: int = 1):
+                        nthreads: int = 1, window: int = 0):
     """testutil.rs:177-218 applied per sequence of a batch (threaded)."""
     q, kc, vc = _f32(q), _f32(kc), _f32(vc)
     pos = np.ascontiguousarray(np.asarray(pos, dtype=np.int32))
@@ -185,13 +204,14 @@ def attn_decode_batched(q, kc, vc, pos, h, hkv, hd, max_seq, cache_stride, scale
     o = np.empty(batch * h * hd, np.float32)
     lib().orc_attn_decode_batched(_p(q), _p(kc), _p(vc), _p(o), batch,
                                   pos.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
-                                  h, hkv, hd, max_seq, cache_stride, float(scale), nthreads)
+                                  h, hkv, hd, max_seq, cache_stride, float(scale), nthreads,
+                                  window)
     return o
 
 
 def attention_prefill(q, k, v, *, seq, h, hkv, hd, max_seq, scale, eps=1e-6,
                       q_norm_w=None, k_norm_w=None, v_norm_w=None, cos=None, sin=None,
-                      kcache=None, vcache=None, cache_round=F32, q_round=F32):
+                      kcache=None, vcache=None, cache_round=F32, q_round=F32, window=0):
     """eyebrowse-nn/src/attention.rs:49-117 after the projections.
     Returns (o, kcache, vcache)."""
     q, k, v = _f32(q), _f32(k), _f32(v)
@@ -203,13 +223,13 @@ def attention_prefill(q, k, v, *, seq, h, hkv, hd, max_seq, scale, eps=1e-6,
     s = None if sin is None else _f32(sin)
     lib().orc_attention_prefill(_p(q), _p(k), _p(v), _p(qn), _p(kn), _p(vn), eps, _p(c), _p(s),
                                 _p(kc), _p(vc), _p(o), seq, h, hkv, hd, max_seq, float(scale),
-                                cache_round, q_round)
+                                cache_round, q_round, window)
     return o, kc, vc
 
 
 def attention_decode(q, k, v, *, pos, h, hkv, hd, max_seq, scale, kcache, vcache, eps=1e-6,
                      q_norm_w=None, k_norm_w=None, v_norm_w=None, cos=None, sin=None,
-                     cache_round=F32):
+                     cache_round=F32, window=0):
     """eyebrowse-nn/src/attention.rs:120-185 after the projections.
     Returns (o, kcache, vcache) with the caches updated at row pos."""
     q, k, v = _f32(q), _f32(k), _f32(v)
@@ -221,7 +241,7 @@ def attention_decode(q, k, v, *, pos, h, hkv, hd, max_seq, scale, kcache, vcache
     s = None if sin is None else _f32(sin)
     lib().orc_attention_decode(_p(q), _p(k), _p(v), _p(qn), _p(kn), _p(vn), eps, _p(c), _p(s),
                                _p(kc), _p(vc), _p(o), pos, h, hkv, hd, max_seq, float(scale),
-                               cache_round)
+                               cache_round, window)
     return o, kc, vc
 
 

@@ -253,8 +253,46 @@ void attention_decode_long_context_hd128() {
   std::vector<float> ones(hd, 1.f), want(n_heads * hd);
   orc_attention_decode(q.data(), k.data(), v.data(), ones.data(), ones.data(), nullptr, 1e-6f,
                        cos.data(), sin.data(), kc.data(), vc.data(), want.data(), pos, n_heads,
-                       n_kv_heads, hd, max_seq, attn.scale, ORC_F32);
+                       n_kv_heads, hd, max_seq, attn.scale, ORC_F32, 0);
   CHECK(max_abs(got, want) <= 2e-3f && rel_l2(got, want) <= 1e-3f, "north-star tolerance");
+}
+
+// Sliding-window layers (Attention::window; the reference defers them):
+// prefill, then a decode step over the cache it wrote, against the oracle's
+// windowed attention (row i sees keys i - window < j <= i).
+void sliding_window_prefill_and_decode() {
+  const size_t n_heads = 8, n_kv_heads = 2, hd = 128, seq = 300, max_seq = 320, window = 100;
+  const size_t q_dim = n_heads * hd, kv_dim = n_kv_heads * hd;
+  nn::Attention attn;
+  attn.n_heads = n_heads;
+  attn.n_kv_heads = n_kv_heads;
+  attn.head_dim = hd;
+  attn.scale = 1.0f / std::sqrt((float)hd);
+  attn.window = window;
+  auto rope = nn::Rope::build(max_seq, hd, 1e6f);
+  auto q = prng(seq * q_dim, 41), k = prng(seq * kv_dim, 42), v = prng(seq * kv_dim, 43);
+  auto kv = nn::KvCache::create(1, max_seq, n_kv_heads, hd);
+  Recorder rec;
+  auto o = attn.prefill(rec, Tensor::from_f32({seq, q_dim}, q), Tensor::from_f32({seq, kv_dim}, k),
+                        Tensor::from_f32({seq, kv_dim}, v), rope, kv, 0, seq);
+  rec.submit();
+  auto got = o.to_f32();
+  auto cos = rope.cos.to_f32(), sin = rope.sin.to_f32();
+  std::vector<float> kc(max_seq * kv_dim, 0.f), vc(max_seq * kv_dim, 0.f), want(seq * q_dim);
+  orc_attention_prefill(q.data(), k.data(), v.data(), nullptr, nullptr, nullptr, 1e-6f,
+                        cos.data(), sin.data(), kc.data(), vc.data(), want.data(), seq, n_heads,
+                        n_kv_heads, hd, max_seq, attn.scale, ORC_F32, ORC_F32, window);
+  CHECK(max_abs(got, want) <= 2e-3f && rel_l2(got, want) <= 1e-3f, "prefill tolerance");
+  auto qd = prng(q_dim, 44), kd = prng(kv_dim, 45), vd = prng(kv_dim, 46);
+  auto od = attn.decode(rec, Tensor::from_f32({1, q_dim}, qd), Tensor::from_f32({1, kv_dim}, kd),
+                        Tensor::from_f32({1, kv_dim}, vd), rope, kv, 0, seq);
+  rec.submit();
+  auto got_d = od.to_f32();
+  std::vector<float> want_d(q_dim);
+  orc_attention_decode(qd.data(), kd.data(), vd.data(), nullptr, nullptr, nullptr, 1e-6f,
+                       cos.data(), sin.data(), kc.data(), vc.data(), want_d.data(), seq, n_heads,
+                       n_kv_heads, hd, max_seq, attn.scale, ORC_F32, window);
+  CHECK(max_abs(got_d, want_d) <= 2e-3f && rel_l2(got_d, want_d) <= 1e-3f, "decode tolerance");
 }
 
 // Where the reference panics on a bad shape, the mirror throws Error.
@@ -288,6 +326,7 @@ int main(int argc, char** argv) {
       {"prefill_decode_consistency", prefill_decode_consistency},
       {"attn_prefill_tensor_core_hd128", attn_prefill_tensor_core_hd128},
       {"attention_decode_long_context_hd128", attention_decode_long_context_hd128},
+      {"sliding_window_prefill_and_decode", sliding_window_prefill_and_decode},
       {"invalid_shapes_throw", invalid_shapes_throw},
   };
   if (argc > 1 && std::string(argv[1]) == "--list") {

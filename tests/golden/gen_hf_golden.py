@@ -9,9 +9,12 @@ apply_rotary_pos_emb and eager_attention_forward -- on seeded inputs, and
 record the post-projection attention output. They pin the oracle's semantics:
 half-split rotation, per-head RMSNorm, GQA head mapping (kv = h // group),
 causal masking, scale, and partial rotary (pairs >= rope_angles pass through).
+The sliding-window cases take their mask from HF's own
+masking_utils.sliding_window_causal_mask_function (Gemma local layers,
+Mistral sliding window); the reference itself has no sliding window yet.
 
-Run from the repo root:  python tests/golden/gen_hf_golden.py
-Writes tests/golden/hf_attn_<case>.npz (a few KB each).
+Run from the repo root:  python tests/golden/gen_hf_golden.py [case ...]
+Writes tests/golden/hf_attn_<case>.npz (a few KB each); all cases by default.
 """
 from __future__ import annotations
 
@@ -20,6 +23,7 @@ import types
 
 import numpy as np
 import torch
+from transformers.masking_utils import causal_mask_function, sliding_window_causal_mask_function
 from transformers.modeling_rope_utils import _compute_proportional_rope_parameters
 from transformers.models.qwen3 import modeling_qwen3 as q3
 
@@ -35,6 +39,13 @@ CASES = {
     # Gemma-4-global-style: QK-norm, weightless V-norm, 25% partial rotary, scale 1.0
     "gemma": dict(seq=10, h=4, hkv=2, hd=64, theta=1e6, qk_norm=True, v_norm=True,
                   partial=0.25, scale=1.0, seed=2),
+    # Gemma-local-style: QK-norm, weightless V-norm, full rotary (theta 1e4),
+    # scale 1.0, sliding window of 7 keys
+    "gemma_local": dict(seq=40, h=4, hkv=2, hd=64, theta=1e4, qk_norm=True, v_norm=True,
+                        partial=1.0, scale=1.0, seed=3, window=7),
+    # Mistral-style sliding window: no norms, full rotary, head_dim 128
+    "mistral_swa": dict(seq=33, h=8, hkv=2, hd=128, theta=1e6, qk_norm=False, v_norm=False,
+                        partial=1.0, scale=None, seed=4, window=16),
 }
 EPS = 1e-6
 
@@ -78,7 +89,12 @@ def make_case(name: str, c: dict) -> None:
     kh = kn.permute(1, 0, 2)[None]
     vh = vn.permute(1, 0, 2)[None]
     qr, kr = q3.apply_rotary_pos_emb(qh, kh, cos[None], sin[None])
-    mask = torch.full((seq, seq), float("-inf")).triu(1)[None, None]
+    window = c.get("window", 0)
+    fn = sliding_window_causal_mask_function(window) if window else causal_mask_function
+    idx = torch.arange(seq)
+    allowed = fn(torch.tensor(0), torch.tensor(0), idx[:, None], idx[None, :])
+    allowed = allowed.expand(seq, seq)
+    mask = torch.zeros(seq, seq).masked_fill(~allowed, float("-inf"))[None, None]
     module = types.SimpleNamespace(num_key_value_groups=h // hkv, training=False)
     out, _ = q3.eager_attention_forward(module, qr, kr, vh, mask, scaling=scale)
     o = out[0]  # [seq, h, hd] after the transpose inside eager_attention_forward
@@ -92,13 +108,14 @@ def make_case(name: str, c: dict) -> None:
     np.savez_compressed(
         os.path.join(HERE, f"hf_attn_{name}.npz"),
         meta=meta, theta=np.float32(c["theta"]), scale=np.float32(scale),
-        eps=np.float32(EPS), v_norm=np.int64(int(c["v_norm"])),
+        eps=np.float32(EPS), v_norm=np.int64(int(c["v_norm"])), window=np.int64(window),
         **{k_: t.detach().contiguous().numpy().astype(np.float32) for k_, t in arrs.items()})
     print(f"wrote hf_attn_{name}.npz (seq={seq} h={h} hkv={hkv} hd={hd} "
-          f"rope_angles={rope_angles} scale={scale:.5f})")
+          f"rope_angles={rope_angles} scale={scale:.5f} window={window})")
 
 
 if __name__ == "__main__":
     torch.set_num_threads(1)
-    for n, c in CASES.items():
-        make_case(n, c)
+    import sys
+    for n in (sys.argv[1:] or list(CASES)):
+        make_case(n, CASES[n])

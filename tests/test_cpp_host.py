@@ -14,7 +14,8 @@ BIN = os.path.join(HERE, "cpp", "_build", "test_attention_path")
 NAMES = ["attn_prefill_matches_cpu", "attn_decode_matches_cpu", "rope_matches_cpu",
          "rmsnorm_matches_cpu", "kv_write_places_rows", "rope_build_tables",
          "prefill_decode_consistency", "attn_prefill_tensor_core_hd128",
-         "attention_decode_long_context_hd128", "invalid_shapes_throw"]
+         "attention_decode_long_context_hd128", "sliding_window_prefill_and_decode",
+         "invalid_shapes_throw"]
 
 
 def _build():

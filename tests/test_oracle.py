@@ -152,7 +152,11 @@ def _load(name):
     return z, seq, h, hkv, hd, rope_angles
 
 
-@pytest.mark.parametrize("name", ["qwen3", "llama", "gemma"])
+def _window(z) -> int:
+    return int(z["window"]) if "window" in z.files else 0
+
+
+@pytest.mark.parametrize("name", ["qwen3", "llama", "gemma", "gemma_local", "mistral_swa"])
 def test_oracle_matches_hf_prefill(orc, name):
     z, seq, h, hkv, hd, ra = _load(name)
     cos, sin = orc.rope_tables(seq, hd, float(z["theta"]), rope_angles=ra)
@@ -162,17 +166,19 @@ def test_oracle_matches_hf_prefill(orc, name):
         scale=float(z["scale"]), eps=float(z["eps"]),
         q_norm_w=z["q_norm_w"] if "q_norm_w" in z else None,
         k_norm_w=z["k_norm_w"] if "k_norm_w" in z else None,
-        v_norm_w=vw, cos=cos, sin=sin)
+        v_norm_w=vw, cos=cos, sin=sin, window=_window(z))
     assert orc.rel_l2(o, z["o"]) < 2e-5
     assert orc.rel_l2(kc, z["k_cache"]) < 2e-6
     assert orc.rel_l2(vc, z["v_cache"]) < 2e-6
 
 
-@pytest.mark.parametrize("name", ["qwen3", "gemma"])
+@pytest.mark.parametrize("name", ["qwen3", "gemma", "gemma_local", "mistral_swa"])
 def test_oracle_decode_steps_match_hf(orc, name):
     """Token-by-token decode through a fresh cache reproduces HF's causal rows
-    (the pattern of eyebrowse-nn/src/tests.rs:181-244)."""
+    (the pattern of eyebrowse-nn/src/tests.rs:181-244). With a sliding window
+    the rows that fell out of it are poisoned before each step."""
     z, seq, h, hkv, hd, ra = _load(name)
+    window = _window(z)
     cos, sin = orc.rope_tables(seq, hd, float(z["theta"]), rope_angles=ra)
     vw = np.ones(hd, np.float32) if int(z["v_norm"]) else None
     kc = np.full(seq * hkv * hd, np.nan, np.float32)   # poison: unwritten rows must not be read
@@ -180,12 +186,17 @@ def test_oracle_decode_steps_match_hf(orc, name):
     q, k, v = (z[n].reshape(seq, -1) for n in ("q", "k", "v"))
     want = z["o"].reshape(seq, -1)
     for pos in range(seq):
-        o, kc, vc = orc.attention_decode(
+        lo = max(0, pos - window + 1) * hkv * hd if window else 0
+        kin, vin = kc.copy(), vc.copy()
+        kin[:lo] = np.nan
+        vin[:lo] = np.nan
+        o, kout, vout = orc.attention_decode(
             q[pos], k[pos], v[pos], pos=pos, h=h, hkv=hkv, hd=hd, max_seq=seq,
-            scale=float(z["scale"]), kcache=kc, vcache=vc, eps=float(z["eps"]),
+            scale=float(z["scale"]), kcache=kin, vcache=vin, eps=float(z["eps"]),
             q_norm_w=z["q_norm_w"] if "q_norm_w" in z else None,
             k_norm_w=z["k_norm_w"] if "k_norm_w" in z else None,
-            v_norm_w=vw, cos=cos, sin=sin)
+            v_norm_w=vw, cos=cos, sin=sin, window=window)
+        kc[lo:], vc[lo:] = kout[lo:], vout[lo:]
         assert orc.rel_l2(o, want[pos]) < 2e-5, pos
     assert orc.rel_l2(kc, z["k_cache"]) < 2e-6
 
