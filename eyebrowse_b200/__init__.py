@@ -28,7 +28,8 @@ EXPORTS = (
     "eb_attention_prefill_gather", "eb_attention_prefill_attend_gather",
     "eb_attention_decode", "eb_attention_decode_batched", "eb_attention_decode_workspace_bytes",
     "eb_workspace_init", "eb_head_concat", "eb_get_device_error",
-    "eb_attention_decode_noalloc", "eb_head_broadcast",
+    "eb_attention_decode_noalloc", "eb_head_broadcast", "eb_linear_f16w",
+    "eb_linear_f16w_workspace_bytes",
 )
 
 
@@ -88,6 +89,9 @@ def lib() -> ctypes.CDLL:
     L.eb_rope.argtypes = [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]
     L.eb_kv_write.argtypes = [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]
     L.eb_rmsnorm.argtypes = [_vp, _vp, _vp, _i64, _i64, _f, _vp]
+    L.eb_linear_f16w.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]
+    L.eb_linear_f16w_workspace_bytes.restype = _sz
+    L.eb_linear_f16w_workspace_bytes.argtypes = [_i64, _i64, _i64]
     L.eb_rope_tables.argtypes = [_vp, _vp, _i64, _i64, _i64, _f]
     dp, lp = ctypes.POINTER(AttnDesc), ctypes.POINTER(AttnLayer)
     L.eb_attention_prefill.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
@@ -180,6 +184,19 @@ def kv_write(cache, src, hkv, count, hd, max_seq, dst_start, stream=None):
 def rmsnorm(x, weight, out, rows, dim, eps, stream=None):
     _check(lib().eb_rmsnorm(_ptr(x), _ptr(weight), _ptr(out), rows, dim, eps, _stream(stream)),
            "eb_rmsnorm")
+
+
+def linear_f16w_workspace_bytes(m, in_f, out_f) -> int:
+    return lib().eb_linear_f16w_workspace_bytes(m, in_f, out_f)
+
+
+def linear_f16w(x, w, y, m, in_f, out_f, workspace=None, stream=None):
+    """eb_linear_f16w: y [m, out_f] = x [m, in_f] (f32) @ w[out_f, in_f]^T (f16),
+    f32 accumulation (linear_f16w, crates/eyebrowse-kernels/src/matmul.rs:128-149).
+    m > 8 needs linear_f16w_workspace_bytes of workspace."""
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _check(lib().eb_linear_f16w(_ptr(x), _ptr(w), _ptr(y), m, in_f, out_f, _ptr(workspace),
+                                ws_bytes, _stream(stream)), "eb_linear_f16w")
 
 
 def rope_tables(max_seq: int, head_dim: int, theta: float, rope_angles: int | None = None):

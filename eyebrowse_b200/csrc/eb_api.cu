@@ -1,6 +1,7 @@
 // eb_api.cu -- the C ABI (include/eyebrowse_attn.h): host-side argument
 // checks, workspace sizing and kernel selection. No call allocates memory.
 #include <math.h>
+#include <stdint.h>
 #include <string.h>
 
 #include <algorithm>
@@ -179,6 +180,11 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
   if (vec) {
     const int es = elem_bytes(d->dtype_cache);
     if (!aligned16(kc) || !aligned16(vc) || ((cache_bstride * es) & 15)) return EB_ERR_INVALID_ARGUMENT;
+    // the new rows are read with 16-byte loads
+    const int eq = elem_bytes(d->dtype_qkv);
+    if (!aligned16(q) || (k && !aligned16(k)) || (v && !aligned16(v)) ||
+        ((q_bstride * eq) & 15) || ((kv_bstride * eq) & 15))
+      return EB_ERR_INVALID_ARGUMENT;
     if (p.cmax > 1 && ((reinterpret_cast<uintptr_t>(ws) & 255) != 0)) return EB_ERR_WORKSPACE;
     DecodeArgs a{};
     a.q = q;
@@ -388,6 +394,30 @@ int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, in
 size_t eb_attn_decode_workspace_bytes(int64_t h, int64_t hkv, int64_t pos, int64_t hd) {
   if (h <= 0 || hkv <= 0 || pos < 0) return 0;
   return decode_workspace_bound(1, h, hkv, hd, kF32, pos);
+}
+
+size_t eb_linear_f16w_workspace_bytes(int64_t m, int64_t in_f, int64_t out_f) {
+  if (m <= 0 || in_f <= 0 || out_f <= 0) return 0;
+  return linear_workspace_bytes(m, in_f, out_f);
+}
+
+int eb_linear_f16w(const float* x, const void* w, float* y, int64_t m, int64_t in_f,
+                   int64_t out_f, void* workspace, size_t workspace_bytes, eb_stream_t stream) {
+  if (m < 0 || in_f <= 0 || out_f <= 0 || in_f > INT32_MAX || out_f > INT32_MAX ||
+      (m + 127) / 128 > 65535)
+    return EB_ERR_INVALID_ARGUMENT;
+  if (m == 0) return EB_OK;
+  if (!x || !w || !y) return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  const LinearPath path = linear_path(m, in_f, out_f, aligned16(x) && aligned16(w) && aligned16(y));
+  if (path == LinearPath::kTensor &&
+      (!workspace || workspace_bytes < linear_workspace_bytes(m, in_f, out_f) ||
+       (reinterpret_cast<uintptr_t>(workspace) & 255)))
+    return EB_ERR_WORKSPACE;
+  unsigned* err = error_word_ptr();
+  if (!err) return EB_ERR_CUDA;
+  return cuda_status(launch_linear(x, w, y, m, in_f, out_f, workspace, path, err,
+                                   reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int eb_attn_decode(const float* q, const float* kcache, const float* vcache, float* o, int64_t h,
@@ -675,7 +705,7 @@ int eb_attention_decode(const eb_attn_desc* d, const eb_attn_layer* L, int64_t p
                         void* o, void* workspace, size_t workspace_bytes, eb_stream_t stream) {
   if (!desc_ok(d) || pos < 0 || pos >= d->max_seq) return EB_ERR_INVALID_ARGUMENT;
   if (!q || !k || !v || !kcache || !vcache || !o) return EB_ERR_INVALID_ARGUMENT;
-  if (d->q_stride || d->kv_stride || d->o_stride) return EB_ERR_UNSUPPORTED;
+  // one row each of q, k, v and o: the row strides do not apply
   if (!device_ok()) return EB_ERR_NO_DEVICE;
   return decode_impl(d, L, 1, nullptr, pos, pos, q, k, v, kcache, vcache, 0, o, 0, 0, 0,
                      workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
@@ -690,14 +720,13 @@ int eb_attention_decode_batched(const eb_attn_desc* d, const eb_attn_layer* L, i
     return EB_ERR_INVALID_ARGUMENT;
   if (batch == 0) return EB_OK;
   if (!positions || !q || !k || !v || !kcache || !vcache || !o) return EB_ERR_INVALID_ARGUMENT;
-  if (d->q_stride || d->kv_stride || d->o_stride) return EB_ERR_UNSUPPORTED;
   if (cache_batch_stride < (int64_t)d->max_seq * d->n_kv_heads * d->head_dim)
     return EB_ERR_INVALID_ARGUMENT;
   if (!device_ok()) return EB_ERR_NO_DEVICE;
-  const int64_t hq = (int64_t)d->n_heads * d->head_dim;
-  const int64_t hk = (int64_t)d->n_kv_heads * d->head_dim;
+  // sequence b's q, k, v and o rows sit b row strides from the first
   return decode_impl(d, L, batch, positions, 0, max_pos, q, k, v, kcache, vcache,
-                     cache_batch_stride, o, hq, hk, hq, workspace, workspace_bytes,
+                     cache_batch_stride, o, qs_of(d), kvs_of(d), os_of(d), workspace,
+                     workspace_bytes,
                      reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -111,6 +111,18 @@ struct DecodeArgs {
 // Returns cudaErrorNotSupported when (hd, cache dtype) has no vector kernel.
 cudaError_t launch_decode(const DecodeArgs& a, int dtype_cache, int batch, cudaStream_t st);
 int decode_rows_per_batch(int hd, int dtype_cache, int group);
+// ------------------------------------------------------------- linear_f16w (eb_linear.cu)
+// y [m, out] = x [m, in] (f32) * w [out, in]^T (f16), f32 accumulation.
+enum class LinearPath { kScalar, kRows, kTensor };
+// kRows for m <= 8, kTensor (tcgen05, needs workspace) above; kScalar when k
+// is not a multiple of 8, a pointer is not 16-byte aligned, or (kTensor) out
+// is not a multiple of 4.
+LinearPath linear_path(int64_t m, int64_t in_f, int64_t out_f, bool aligned);
+size_t linear_workspace_bytes(int64_t m, int64_t in_f, int64_t out_f);
+cudaError_t launch_linear(const float* x, const void* w, float* y, int64_t m, int64_t in_f,
+                          int64_t out_f, void* ws, LinearPath path, unsigned* err,
+                          cudaStream_t st);
+
 // tcgen05 decode for 16-bit caches (eb_decode_tc.cu)
 bool decode_tc_supported(int hd, int dtype_cache, int group);
 cudaError_t launch_decode_tc(const DecodeArgs& a, int dtype_cache, int batch, cudaStream_t st);

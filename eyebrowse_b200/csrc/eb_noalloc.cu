@@ -54,7 +54,6 @@ extern "C" int eb_attention_decode_noalloc(const eb_attn_desc* d, const eb_attn_
       pos >= d->max_seq || d->window < 0)
     return EB_ERR_INVALID_ARGUMENT;
   if (!q || !k || !v || !kcache || !vcache || !o) return EB_ERR_INVALID_ARGUMENT;
-  if (d->q_stride || d->kv_stride || d->o_stride) return EB_ERR_UNSUPPORTED;
   // The split-K plan for this shape must fit the fixed scratch; refuse, before
   // touching the device, a shape whose partials would not.
   const size_t need = decode_plan_bytes(d, 1, pos);

@@ -91,18 +91,6 @@ struct GatherMaps {
   CUtensorMap m[kMaxGather];
 };
 
-// Named barrier over n threads that also ANDs a predicate across them, so
-// every participant takes the same branch afterwards.
-__device__ __forceinline__ bool named_bar_and(int id, int n, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)v), "r"(id), "r"(n)
-      : "memory");
-  return r != 0;
-}
 
 
 

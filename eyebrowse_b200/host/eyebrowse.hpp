@@ -18,6 +18,7 @@
 // carrying the C ABI's status string.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -67,6 +68,16 @@ class Tensor {
     Tensor t = empty(std::move(shape), DType::F32);
     if (host.size() != t.numel()) throw Error("Tensor::from_f32: size mismatch", EB_ERR_INVALID_ARGUMENT);
     check_cuda(cudaMemcpy(t.ptr(), host.data(), t.bytes(), cudaMemcpyHostToDevice), "cudaMemcpy");
+    return t;
+  }
+  // f16 weights from f32 host values (round to nearest even), as the
+  // reference's pack_f16 stores them (testutil.rs:45-60)
+  static Tensor from_f16(std::vector<size_t> shape, const std::vector<float>& host) {
+    Tensor t = empty(std::move(shape), DType::F16);
+    if (host.size() != t.numel()) throw Error("Tensor::from_f16: size mismatch", EB_ERR_INVALID_ARGUMENT);
+    std::vector<__half> h(host.size());
+    for (size_t i = 0; i < host.size(); i++) h[i] = __float2half_rn(host[i]);
+    check_cuda(cudaMemcpy(t.ptr(), h.data(), t.bytes(), cudaMemcpyHostToDevice), "cudaMemcpy");
     return t;
   }
   static Tensor zeros(std::vector<size_t> shape, DType dt = DType::F32) {
@@ -125,7 +136,13 @@ class Recorder {
   std::vector<Tensor> ws_;
 };
 
-enum WorkspaceKind { kWsPrefill = 0, kWsDecode = 1, kWsKernelPrefill = 2, kWsKernelDecode = 3 };
+enum WorkspaceKind {
+  kWsPrefill = 0,
+  kWsDecode = 1,
+  kWsKernelPrefill = 2,
+  kWsKernelDecode = 3,
+  kWsLinear = 4
+};
 
 // ------------------------------------------------------------ eyebrowse-kernels
 namespace kernels {
@@ -178,6 +195,15 @@ inline void rmsnorm(Recorder& rec, const Tensor& x, const Tensor& weight, const 
         "rmsnorm");
 }
 
+// matmul.rs:128-149: c [m, out_f] = a [m, in_f] (f32) * w [out_f, in_f]^T (f16 HF layout).
+inline void linear_f16w(Recorder& rec, const Tensor& a, const Tensor& w, const Tensor& c,
+                        size_t m, size_t in_f, size_t out_f) {
+  auto ws = rec.workspace(kWsLinear, eb_linear_f16w_workspace_bytes(m, in_f, out_f));
+  check(eb_linear_f16w(static_cast<const float*>(a.ptr()), w.ptr(), static_cast<float*>(c.ptr()),
+                       m, in_f, out_f, ws.first, ws.second, rec.stream()),
+        "linear_f16w");
+}
+
 }  // namespace kernels
 
 // ------------------------------------------------------------ eyebrowse-nn
@@ -221,6 +247,18 @@ struct KvCache {
       c.v.push_back(Tensor::zeros({max_seq, n_kv_heads, head_dim}, dtype));
     }
     return c;
+  }
+};
+
+// linear.rs:5-23: a bias-free linear layer, f16 weights [out_f, in_f].
+struct Linear {
+  Tensor w;
+  size_t in_f = 0, out_f = 0;
+  // x [rows, in_f] f32 -> [rows, out_f] f32
+  Tensor forward(Recorder& rec, const Tensor& x, size_t rows) const {
+    Tensor out = Tensor::empty({rows, out_f});
+    kernels::linear_f16w(rec, x, w, out, rows, in_f, out_f);
+    return out;
   }
 };
 

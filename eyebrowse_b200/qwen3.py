@@ -19,10 +19,12 @@ RoPE theta 1e6, GQA 16/8, head_dim 128).
 What runs where: every layer's attention -- QK-norm, RoPE, the KV-cache
 write, the causal prefill over the prompt and each single-token decode step
 -- goes through this library's C ABI (eb_attention_prefill /
-eb_attention_decode on f32 caches, the tensor-core path), and the block and
-final RMSNorms through eb_rmsnorm. The projections, SwiGLU, the embedding
-gather and the argmax are plain f32 torch operations (cuBLAS GEMMs with
-TF32 off): they are outside the attention path this library replaces.
+eb_attention_decode on f32 caches, the tensor-core path); every projection
+through eb_linear_f16w: one fused q/k/v GEMM whose output rows the attention
+reads in place (q_stride = kv_stride = the fused width), o_proj, one fused
+gate/up GEMM, down_proj and the tied LM head; the block and final RMSNorms
+through eb_rmsnorm. The embedding gather, the residual adds, SiLU * up and
+the argmax are plain torch element-wise operations.
 """
 from __future__ import annotations
 
@@ -86,21 +88,37 @@ class GreedyModel:
         import eyebrowse_b200 as eb
         self.eb, self.g, self.max_seq = eb, geometry, max_seq
         g = geometry
-        torch.backends.cuda.matmul.allow_tf32 = False
         dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
-        self.W = {k: dev(v) for k, v in weights.items()}
-        H, Hkv, hd = g["heads"], g["kv_heads"], g["head_dim"]
+        f16 = lambda *names: dev(np.concatenate([weights[n] for n in names]).astype(np.float16))
+        H, Hkv, hd, D, inter = g["heads"], g["kv_heads"], g["head_dim"], g["hidden"], g["inter"]
+        self.qkv_w = (H + 2 * Hkv) * hd  # fused q/k/v output width
+        self.norms = {k: dev(v) for k, v in weights.items() if k.endswith("norm.weight")}
+        self.embed = dev(weights["model.embed_tokens.weight"])      # f32 rows for the gather
+        self.lm_head = f16("model.embed_tokens.weight")             # tied, f16 [vocab, hidden]
+        self.lin = []
+        for i in range(g["layers"]):
+            p = f"model.layers.{i}"
+            self.lin.append(dict(
+                qkv=f16(f"{p}.self_attn.q_proj.weight", f"{p}.self_attn.k_proj.weight",
+                        f"{p}.self_attn.v_proj.weight"),
+                o=f16(f"{p}.self_attn.o_proj.weight"),
+                gate_up=f16(f"{p}.mlp.gate_proj.weight", f"{p}.mlp.up_proj.weight"),
+                down=f16(f"{p}.mlp.down_proj.weight")))
         cos, sin = eb.rope_tables(max_seq, hd, g["theta"])
         self.cos, self.sin = dev(cos), dev(sin)
-        self.desc = eb.make_desc(H, Hkv, hd, max_seq, eps=g["eps"])
+        self.desc = eb.make_desc(H, Hkv, hd, max_seq, eps=g["eps"], q_stride=self.qkv_w,
+                                 kv_stride=self.qkv_w)
         self.layers = [
-            eb.make_layer(self.W[f"model.layers.{i}.self_attn.q_norm.weight"],
-                          self.W[f"model.layers.{i}.self_attn.k_norm.weight"], None,
+            eb.make_layer(self.norms[f"model.layers.{i}.self_attn.q_norm.weight"],
+                          self.norms[f"model.layers.{i}.self_attn.k_norm.weight"], None,
                           self.cos, self.sin) for i in range(g["layers"])]
         self.ws_prefill = eb.alloc_workspace(eb.attention_prefill_workspace_bytes(self.desc,
                                                                                   max_seq))
         self.ws_decode = eb.alloc_workspace(eb.attention_decode_workspace_bytes(self.desc, 1,
                                                                                 max_seq - 1))
+        nb = max(eb.linear_f16w_workspace_bytes(max_seq, k, n)
+                 for k, n in ((D, self.qkv_w), (H * hd, D), (D, 2 * inter), (inter, D)))
+        self.ws_linear = eb.alloc_workspace(nb) if nb else None
         self.reset()
 
     def reset(self):
@@ -116,21 +134,29 @@ class GreedyModel:
         self.eb.rmsnorm(x, w, out, x.shape[0], x.shape[1], self.g["eps"])
         return out
 
+    def _linear(self, x, w):
+        """eb_linear_f16w: x [rows, in] f32 @ w [out, in]^T (f16) -> [rows, out] f32."""
+        import torch
+        rows, in_f = x.shape
+        out_f = w.shape[0]
+        y = torch.empty(rows, out_f, device="cuda")
+        self.eb.linear_f16w(x, w, y, rows, in_f, out_f, self.ws_linear)
+        return y
+
     def _forward(self, ids, base_pos: int):
         """Hidden state of the last row after the final norm; ids at positions
         base_pos.. (a prompt at 0, or one token at base_pos)."""
         import torch
-        g, W, eb = self.g, self.W, self.eb
+        g, N, eb = self.g, self.norms, self.eb
         rows = len(ids)
-        H, hd = g["heads"], g["head_dim"]
-        x = W["model.embed_tokens.weight"][torch.tensor(ids, device="cuda")].contiguous()
+        H, Hkv, hd, inter = g["heads"], g["kv_heads"], g["head_dim"], g["inter"]
+        x = self.embed[torch.tensor(ids, device="cuda")].contiguous()
         o = torch.empty(rows, H, hd, device="cuda")
         for i in range(g["layers"]):
-            p = f"model.layers.{i}"
-            h = self._norm(x, W[f"{p}.input_layernorm.weight"])
-            q = (h @ W[f"{p}.self_attn.q_proj.weight"].T).contiguous()
-            k = (h @ W[f"{p}.self_attn.k_proj.weight"].T).contiguous()
-            v = (h @ W[f"{p}.self_attn.v_proj.weight"].T).contiguous()
+            p, L = f"model.layers.{i}", self.lin[i]
+            h = self._norm(x, N[f"{p}.input_layernorm.weight"])
+            qkv = self._linear(h, L["qkv"])  # rows of [q | k | v], read in place
+            q, k, v = qkv[:, :H * hd], qkv[:, H * hd:(H + Hkv) * hd], qkv[:, (H + Hkv) * hd:]
             if base_pos == 0:
                 eb.attention_prefill(self.desc, self.layers[i], rows, q, k, v, self.kc[i],
                                      self.vc[i], o, self.ws_prefill)
@@ -138,17 +164,16 @@ class GreedyModel:
                 assert rows == 1
                 eb.attention_decode(self.desc, self.layers[i], base_pos, q, k, v, self.kc[i],
                                     self.vc[i], o, self.ws_decode)
-            x = x + o.view(rows, H * hd) @ W[f"{p}.self_attn.o_proj.weight"].T
-            h2 = self._norm(x, W[f"{p}.post_attention_layernorm.weight"])
-            gt = h2 @ W[f"{p}.mlp.gate_proj.weight"].T
-            up = h2 @ W[f"{p}.mlp.up_proj.weight"].T
-            x = x + ((gt / (1.0 + torch.exp(-gt))) * up) @ W[f"{p}.mlp.down_proj.weight"].T
-        return self._norm(x[-1:].contiguous(), W["model.norm.weight"])
+            x = x + self._linear(o.view(rows, H * hd), L["o"])
+            h2 = self._norm(x, N[f"{p}.post_attention_layernorm.weight"])
+            gu = self._linear(h2, L["gate_up"])
+            gt, up = gu[:, :inter], gu[:, inter:]
+            x = x + self._linear(((gt / (1.0 + torch.exp(-gt))) * up).contiguous(), L["down"])
+        return self._norm(x[-1:].contiguous(), N["model.norm.weight"])
 
     def logits(self, ids, base_pos: int):
         """[vocab] logits after ids at positions base_pos.. (updates the caches)."""
-        xn = self._forward(ids, base_pos)
-        return (xn @ self.W["model.embed_tokens.weight"].T)[0]
+        return self._linear(self._forward(ids, base_pos), self.lm_head)[0]
 
     def next_id(self, ids, base_pos: int) -> int:
         import torch

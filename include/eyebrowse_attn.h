@@ -103,6 +103,25 @@ EB_API int eb_rope_tables(float* cos_t, float* sin_t, int64_t max_seq, int64_t h
                    int64_t rope_angles, float theta);
 
 /* ------------------------------------------------------------------------ *
+ * The projections around the path: linear_f16w
+ * (crates/eyebrowse-kernels/src/matmul.rs:128-149), the GEMM of eyebrowse-nn
+ * Linear::forward (crates/eyebrowse-nn/src/linear.rs:17-22).
+ * y [m, out_f] = x [m, in_f] (f32) * w [out_f, in_f]^T with w f16 in the HF
+ * layout (the reference's packed-u32 f16 pairs are the same bytes) and f32
+ * accumulation. m <= 8 streams w once (HBM-bound); larger m runs on the
+ * tensor cores with x split into f16 hi/lo planes, which needs
+ * eb_linear_f16w_workspace_bytes of workspace (256-byte aligned) and
+ * |x| < 65504. A fused projection is one call over concatenated weights:
+ * w = [Wq; Wk; Wv] gives rows [q | k | v] that eb_attention_* read in place
+ * (q = y, k = y + n_heads*head_dim, v = k + n_kv_heads*head_dim,
+ * q_stride = kv_stride = out_f).
+ * ------------------------------------------------------------------------ */
+EB_API size_t eb_linear_f16w_workspace_bytes(int64_t m, int64_t in_f, int64_t out_f);
+EB_API int eb_linear_f16w(const float* x, const void* w, float* y, int64_t m, int64_t in_f,
+                          int64_t out_f, void* workspace, size_t workspace_bytes,
+                          eb_stream_t stream);
+
+/* ------------------------------------------------------------------------ *
  * The fused attention primitive: the body of eyebrowse-nn Attention::prefill
  * and Attention::decode between the projections and o_proj
  * (crates/eyebrowse-nn/src/attention.rs:62-115 and :133-183): optional
@@ -202,7 +221,9 @@ EB_API int eb_attention_prefill_attend_gather(const eb_attn_desc* desc,
  * crates/eyebrowse-nn/src/attention.rs:120-185): q [n_heads, head_dim],
  * k/v [n_kv_heads, head_dim] are the projection outputs of the new token; the
  * processed k/v are written to cache row pos and attention runs over rows
- * 0..=pos into o [n_heads, head_dim]. */
+ * 0..=pos (the last `window` of them with a sliding window) into
+ * o [n_heads, head_dim]. One row each: the descriptor's row strides do not
+ * apply. q, k and v start on 16-byte boundaries. */
 EB_API int eb_attention_decode(const eb_attn_desc* desc, const eb_attn_layer* layer, int64_t pos,
                         const void* q, const void* k, const void* v, void* kcache, void* vcache,
                         void* o, void* workspace, size_t workspace_bytes, eb_stream_t stream);
@@ -211,7 +232,9 @@ EB_API int eb_attention_decode(const eb_attn_desc* desc, const eb_attn_layer* la
  * kcache + b*cache_batch_stride elements (same for vcache) and its own
  * position positions[b] (DEVICE array of int32, every value < max_seq and
  * <= max_pos). q/o are [batch, n_heads, head_dim]; k/v [batch, n_kv_heads,
- * head_dim]. No reference counterpart: the reference decodes one sequence. */
+ * head_dim], with sequence b's rows b * q_stride / kv_stride / o_stride
+ * elements from the first (16-byte multiples for q, k and v). No reference
+ * counterpart: the reference decodes one sequence. */
 EB_API int eb_attention_decode_batched(const eb_attn_desc* desc, const eb_attn_layer* layer,
                                 int64_t batch, const int32_t* positions, int64_t max_pos,
                                 const void* q, const void* k, const void* v, void* kcache,

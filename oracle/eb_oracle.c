@@ -170,6 +170,19 @@ void orc_kv_write(float* cache, const float* src, size_t hkv, size_t count, size
   }
 }
 
+/* crates/eyebrowse-kernels/src/testutil.rs:66-79 (cpu_linear): y[m, o] =
+ * sum over k in order of x[m, k] * w[o, k], one f32 accumulator, multiply and
+ * add rounded separately (the file is built with -ffp-contract=off). w holds
+ * the f16-rounded weights as f32 (the reference rounds them with round_f16). */
+void orc_linear(const float* x, const float* w, float* y, size_t m, size_t in_f, size_t out_f) {
+  for (size_t i = 0; i < m; i++)
+    for (size_t o = 0; o < out_f; o++) {
+      float acc = 0.0f;
+      for (size_t k = 0; k < in_f; k++) acc += x[i * in_f + k] * w[o * in_f + k];
+      y[i * out_f + o] = acc;
+    }
+}
+
 /* One (query row, head) of the two-pass attention in testutil.rs:142-169.
  * `scores` has room for n_keys floats. */
 static void attn_row(const float* qrow, const float* k, const float* v, float* orow,

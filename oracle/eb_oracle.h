@@ -63,6 +63,11 @@ void orc_rope_tables(float* cos_t, float* sin_t, size_t max_seq, size_t hd,
 void orc_kv_write(float* cache, const float* src, size_t hkv, size_t count, size_t hd,
                   size_t max_seq, size_t dst_start);
 
+/* Linear layer, HF layout w [out_f, in_f]: y [m, out_f] = x w^T.
+ * crates/eyebrowse-kernels/src/testutil.rs:66-79 (cpu_linear), the CPU
+ * reference of linear_f16w (matmul.rs:128-149) with f16-rounded w. */
+void orc_linear(const float* x, const float* w, float* y, size_t m, size_t in_f, size_t out_f);
+
 /* Causal GQA attention, seq-major: q [s,h,hd], k/v [s,hkv,hd] -> o [s,h,hd].
  * crates/eyebrowse-kernels/src/testutil.rs:130-172 (two-pass softmax, f32 dot
  * accumulated over d in order, then *= scale). */

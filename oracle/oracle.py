@@ -50,6 +50,7 @@ def lib():
         L.orc_rope.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz]
         L.orc_rope_tables.argtypes = [_fp, _fp, _sz, _sz, _sz, ctypes.c_float]
         L.orc_kv_write.argtypes = [_fp, _fp, _sz, _sz, _sz, _sz, _sz]
+        L.orc_linear.argtypes = [_fp, _fp, _fp, _sz, _sz, _sz]
         L.orc_attn_prefill.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz, ctypes.c_float]
         L.orc_attn_prefill_window.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz,
                                               ctypes.c_float, _sz]
@@ -149,6 +150,15 @@ def kv_write(cache, src, hkv: int, count: int, hd: int, max_seq: int, dst_start:
     src = _f32(src)
     lib().orc_kv_write(_p(cache), _p(src), hkv, count, hd, max_seq, dst_start)
     return cache
+
+
+def linear(x, w, m: int, in_f: int, out_f: int) -> np.ndarray:
+    """testutil.rs:66-79 (cpu_linear): y [m, out_f] = x [m, in_f] @ w [out_f, in_f]^T,
+    f32, k summed in order. Pass w already rounded to f16 (round_f16)."""
+    x, w = _f32(x), _f32(w)
+    y = np.empty(m * out_f, np.float32)
+    lib().orc_linear(_p(x), _p(w), _p(y), m, in_f, out_f)
+    return y
 
 
 def attn_prefill(q, k, v, h: int, hkv: int, s: int, hd: int, scale: float | None = None,

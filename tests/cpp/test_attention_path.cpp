@@ -8,6 +8,7 @@
 //   kv_write_places_rows        crates/eyebrowse-kernels/src/ops.rs:272-292
 //   rope_build_tables           crates/eyebrowse-nn/src/tests.rs:152-176
 //   prefill_decode_consistency  crates/eyebrowse-nn/src/tests.rs:181-244
+//   linear_f16w_matches_cpu     crates/eyebrowse-kernels/src/matmul.rs:261-279
 //       (here from the projection outputs on, with the same prng seeds)
 // plus tensor-core-sized cases at the north-star tolerance and the error
 // behaviour. The CPU side is the C oracle (oracle/eb_oracle.c), the
@@ -295,6 +296,46 @@ void sliding_window_prefill_and_decode() {
   CHECK(max_abs(got_d, want_d) <= 2e-3f && rel_l2(got_d, want_d) <= 1e-3f, "decode tolerance");
 }
 
+// crates/eyebrowse-kernels/src/matmul.rs:261-279: in_f not a multiple of 16,
+// f16 weights, against cpu_linear on the f16-rounded weights.
+void linear_f16w_matches_cpu() {
+  const size_t m = 5, in_f = 33, out_f = 7;
+  auto x = ramp(m * in_f, -0.2f, 0.01f), w = ramp(out_f * in_f, -0.3f, 0.005f);
+  auto ct = Tensor::empty({m, out_f});
+  Recorder rec;
+  kernels::linear_f16w(rec, Tensor::from_f32({m, in_f}, x), Tensor::from_f16({out_f, in_f}, w), ct,
+                       m, in_f, out_f);
+  rec.submit();
+  auto got = ct.to_f32();
+  orc_round_f16(w.data(), w.size());
+  std::vector<float> want(m * out_f);
+  orc_linear(x.data(), w.data(), want.data(), m, in_f, out_f);
+  CHECK(rel_l2(got, want) < 2e-3f, "rel_l2");
+}
+
+// nn::Linear on both device kernels: a decode row (m = 1, streamed weights)
+// and a prefill block (m = 200, tensor cores), fused q/k/v width.
+void linear_forward_decode_and_prefill() {
+  const size_t in_f = 1024, out_f = 4096;
+  nn::Linear lin;
+  auto w = prng(out_f * in_f, 51);
+  for (auto& v : w) v *= 0.05f;
+  lin.w = Tensor::from_f16({out_f, in_f}, w);
+  lin.in_f = in_f;
+  lin.out_f = out_f;
+  orc_round_f16(w.data(), w.size());
+  Recorder rec;
+  for (size_t m : {size_t(1), size_t(200)}) {
+    auto x = prng(m * in_f, 52 + m);
+    auto y = lin.forward(rec, Tensor::from_f32({m, in_f}, x), m);
+    rec.submit();
+    auto got = y.to_f32();
+    std::vector<float> want(m * out_f);
+    orc_linear(x.data(), w.data(), want.data(), m, in_f, out_f);
+    CHECK(rel_l2(got, want) < 1e-5f, "rel_l2 vs cpu_linear");
+  }
+}
+
 // Where the reference panics on a bad shape, the mirror throws Error.
 void invalid_shapes_throw() {
   auto x = Tensor::zeros({64});
@@ -327,6 +368,8 @@ int main(int argc, char** argv) {
       {"attn_prefill_tensor_core_hd128", attn_prefill_tensor_core_hd128},
       {"attention_decode_long_context_hd128", attention_decode_long_context_hd128},
       {"sliding_window_prefill_and_decode", sliding_window_prefill_and_decode},
+      {"linear_f16w_matches_cpu", linear_f16w_matches_cpu},
+      {"linear_forward_decode_and_prefill", linear_forward_decode_and_prefill},
       {"invalid_shapes_throw", invalid_shapes_throw},
   };
   if (argc > 1 && std::string(argv[1]) == "--list") {

@@ -124,6 +124,21 @@ def test_rmsnorm_ramp(orc):
     assert orc.rel_l2(got, want.ravel()) < 1e-6
 
 
+def test_linear_ramp(orc):
+    # crates/eyebrowse-kernels/src/matmul.rs:261-279 inputs (in_f not a multiple of 16)
+    m, in_f, out_f = 5, 33, 7
+    x = orc.ramp(m * in_f, -0.2, 0.01)
+    w = orc.round_f16(orc.ramp(out_f * in_f, -0.3, 0.005))
+    got = orc.linear(x, w, m, in_f, out_f)
+    want = x.reshape(m, in_f).astype(np.float64) @ w.reshape(out_f, in_f).astype(np.float64).T
+    assert orc.rel_l2(got, want.ravel()) < 1e-6
+    # k summed in order in one f32 accumulator, multiply and add rounded apart
+    acc = np.float32(0)
+    for k in range(in_f):
+        acc = np.float32(acc + np.float32(x[k] * w[k]))
+    assert got[0] == acc
+
+
 def test_attn_prefill_ramp(orc):
     # crates/eyebrowse-kernels/src/attention.rs:174-202 inputs
     h, hkv, s, hd = 2, 1, 5, 8
