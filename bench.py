@@ -506,6 +506,90 @@ class DecodeWork:
         return self.bytes_total()
 
 
+class LinearWork:
+    """The projections around the path (linear_f16w through eb_linear_f16w):
+    y [m, n] = x [m, k] (f32) @ w [n, k]^T (f16). m > 8 runs on the tensor
+    cores (x as f16 hi + lo planes: 2 * 2mnk MMA FLOP per 2mnk of algorithmic
+    work) and is reported in TFLOP/s; m <= 8 streams w and is reported in
+    GB/s. The weights stay resident (they are the model); the e2e step copies
+    x in from pinned host memory and y back."""
+
+    def __init__(self, name, m, k, n, seed=6):
+        self.name, self.m, self.k, self.n, self.seed = name, m, k, n, seed
+        self.bound = "tensor" if m > 8 else "hbm"
+
+    def describe(self, world):
+        return {"workload": self.name, "m": self.m, "in_features": self.k,
+                "out_features": self.n, "weights": "f16", "activations": "f32",
+                "parallelism": "1 GPU (replicas)" if world > 1 else "1 GPU"}
+
+    def flops(self):
+        return 2.0 * self.m * self.n * self.k
+
+    def bytes_total(self):
+        return 2.0 * self.n * self.k + 4.0 * self.m * (self.k + self.n)
+
+    def setup(self, rank, world):
+        import torch
+
+        import eyebrowse_b200 as eb
+        self.eb, self.world = eb, world
+        g = torch.Generator(device="cuda").manual_seed(self.seed)
+        self.x = torch.randn(self.m, self.k, device="cuda", generator=g)
+        self.w = (torch.randn(self.n, self.k, device="cuda", generator=g) * 0.02).half()
+        self.y = torch.empty(self.m, self.n, device="cuda")
+        nb = eb.linear_f16w_workspace_bytes(self.m, self.k, self.n)
+        self.ws = eb.alloc_workspace(nb) if nb else None
+        self.launches_per_step = 2 if nb else 1  # split of x + GEMM, or the GEMV
+        self.full = self.y
+
+    def step(self):
+        self.eb.linear_f16w(self.x, self.w, self.y, self.m, self.k, self.n, self.ws)
+
+    kernel_only = step
+
+    def kernel_units(self):
+        return self.flops() if self.bound == "tensor" else self.bytes_total()
+
+    def e2e(self, rank, world, steps, unit):
+        import torch
+        hx = self.x.cpu().pin_memory()
+        hy = torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
+
+        def st():
+            self.x.copy_(hx, non_blocking=True)
+            self.step()
+            hy.copy_(self.y, non_blocking=True)
+        ems, _ = time_steps(st, steps, 2, world)
+        units = self.flops() / 1e12 if self.bound == "tensor" else self.bytes_total() / 1e9
+        return {"value": units / (ems / steps * 1e-3), "unit": unit,
+                "h2d_bytes_per_step": int(hx.numel() * 4), "d2h_bytes_per_step": int(hy.numel() * 4)}
+
+
+def cpu_baseline_linear(w: LinearWork, threads: int | None = None, target_s: float = 8.0):
+    """Oracle cpu_linear (single thread, the reference's loop order) over a
+    bounded sample of output columns, scaled to the workload's unit."""
+    from oracle import oracle as orc
+    rng = np.random.default_rng(0)
+    m = min(w.m, 8)
+    x = rng.standard_normal((m, w.k)).astype(np.float32)
+    n = min(w.n, 256)
+    while True:
+        wt = (rng.standard_normal((n, w.k)) * 0.02).astype(np.float16).astype(np.float32)
+        t0 = time.perf_counter()
+        orc.linear(x, wt, m, w.k, n)
+        dt = time.perf_counter() - t0
+        if dt >= target_s / 4 or n >= w.n:
+            break
+        n = min(w.n, int(n * max(2.0, target_s / 2 / max(dt, 1e-4))))
+    flop, nbytes = 2.0 * m * n * w.k, 2.0 * n * w.k
+    value = flop / dt / 1e12 if w.bound == "tensor" else nbytes / dt / 1e9
+    return {"value": value, "unit": "TFLOP/s" if w.bound == "tensor" else "GB/s", "cores": 1,
+            "kind": "port",
+            "sample": f"oracle cpu_linear, {m} rows x {n} of {w.n} outputs, k={w.k} "
+                      f"({dt:.2f} s, f32, gcc -O3 -ffp-contract=off, 1 thread)"}
+
+
 def make_workload(name, batch=None):
     if name == "cfg1":
         return PrefillWork("cfg1 causal GQA prefill S128 H16 Hkv8 hd128 f32 (Qwen3-0.6B layer)",
@@ -525,6 +609,12 @@ def make_workload(name, batch=None):
                           v_norm=True, scale=1.0, rope_angles=32, n_rot=8)
     if name == "cfg5":
         return BatchedDecodeWork(B=batch or 64)
+    if name == "proj3":
+        return LinearWork("proj3 fused q/k/v projection S8192 hidden 4096 -> (32+2x8)x128 "
+                          "(Llama-3-8B layer, config 3's geometry)", 8192, 4096, 6144)
+    if name == "projd":
+        return LinearWork("projd tied LM head, one decode row: 1024 -> 151936 "
+                          "(Qwen3-0.6B geometry)", 1, 1024, 151936)
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -644,8 +734,10 @@ def run_reference(args):
             fixed = b["_sample"]
         elif isinstance(w, BatchedDecodeWork):
             b = cpu_baseline_decode(w, threads=threads, n_seq=2)
+        elif isinstance(w, LinearWork):
+            b = cpu_baseline_linear(w, target_s=per_step)
         else:
-            raise SystemExit("--impl reference supports cfg1, cfg3, cfg4, cfg5")
+            raise SystemExit("--impl reference supports cfg1, cfg3, cfg4, cfg5, proj3, projd")
         if i >= args.warmup:
             vals.append(b["value"])
             base = b
@@ -660,7 +752,8 @@ def run_reference(args):
             "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "note": "reference = oracle/ C restatement of crates/eyebrowse-kernels/src/testutil.rs "
-                    "CPU attention; the Rust/wgpu reference cannot be built or run on this box"}
+                    "CPU attention (cpu_linear for proj3/projd); the Rust/wgpu reference cannot "
+                    "be built or run on this box"}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -747,7 +840,8 @@ def main():
     w = make_workload(args.workload, args.batch)
     res = measure(w, rank, world, args.steps, args.warmup, peaks, peak_kind, sampler)
     is_prefill = isinstance(w, PrefillWork)
-    if is_prefill:
+    is_tensor = is_prefill or getattr(w, "bound", "") == "tensor"
+    if is_tensor:
         total_units = w.flops()
         unit, bound = "TFLOP/s", "tensor"
         value = total_units / (res["ms_per_step"] * 1e-3) / 1e12
@@ -767,7 +861,9 @@ def main():
 
     # e2e: the same step through the public API with host buffers
     e2e = None
-    if is_prefill:
+    if hasattr(w, "e2e"):
+        e2e = w.e2e(rank, world, args.e2e_steps, unit)
+    elif is_prefill:
         w.setup_e2e()
         bi = bo = 0
 
@@ -810,11 +906,14 @@ def main():
             cpu.pop("_sample", None)
         elif isinstance(w, BatchedDecodeWork):
             cpu = cpu_baseline_decode(w)
+        elif isinstance(w, LinearWork):
+            cpu = cpu_baseline_linear(w)
 
     launches = w.launches_per_step * args.steps
     if rank == 0:
         tkey = {"cfg3": "prefill_cfg3", "cfg1": "prefill_cfg1", "cfg4": "prefill_cfg4",
-                "cfg2": "decode_cfg2", "cfg5": "decode_cfg5"}.get(args.workload)
+                "cfg2": "decode_cfg2", "cfg5": "decode_cfg5", "proj3": "linear_proj3",
+                "projd": "linear_projd"}.get(args.workload)
         line = {
             "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
@@ -822,7 +921,7 @@ def main():
             "dtype": {0: "f32", 1: "f16", 2: "bf16"}.get(getattr(w, "dt", 0), "f32"),
             "data": "synthetic (seeded N(0,1) inputs of the config's shapes; no dataset)",
             "config": dict(w.describe(world), l2="inputs larger than L2 (no flush)"
-                           if is_prefill or isinstance(w, BatchedDecodeWork)
+                           if is_prefill or isinstance(w, (BatchedDecodeWork, LinearWork))
                            else "rotating caches larger than L2",
                            untimed_warm_s=WARM_S),
             "cuda_graph_steps": res.get("graph_reps", 0),

@@ -8,9 +8,9 @@
 //
 // Three kernels, chosen by the host:
 // - linear_rows_kernel (m <= 8: decode steps, the LM head). HBM-bound on w:
-//   each CTA owns 4 output rows and streams them once with 16-byte loads,
-//   the k range spread over its threads, every load of a pass in flight
-//   before any use; x comes through L1. f32 FMA per product.
+//   each warp owns 1 or 4 output rows and streams them once with 16-byte
+//   loads, 4 per row in flight per lane; x comes through L1. f32 FMA per
+//   product, a warp reduction per output.
 // - linear_tc_kernel (m > 8: prefill). tcgen05 with f32 accumulation in
 //   TMEM, 128 x 256 output tiles, a 3-stage TMA ring over 64-wide k chunks.
 //   x is first split into f16 hi and lo planes (split_x_kernel); every tile
@@ -34,45 +34,45 @@
 namespace eb {
 
 // ---------------------------------------------------------------- m <= 8
-constexpr int kRowsThreads = 256;
-constexpr int kRowsPerCta = 4;
-constexpr int kRowsUnroll = 2;  // 8-element k chunks per thread per pass
+// One warp owns R output rows over the whole k range: lane l takes the
+// 8-element chunks l, l+32, ..., B chunks per row in flight per pass; a warp
+// reduction finishes each dot product (no shared memory, no block barrier).
+constexpr int kRowsWarps = 8;
+constexpr int kRowsBatch = 4;
 
-template <int MR>
-__global__ void __launch_bounds__(kRowsThreads) linear_rows_kernel(const float* __restrict__ x,
-                                                                   const __half* __restrict__ w,
-                                                                   float* __restrict__ y, int m,
-                                                                   int in_f, int out_f) {
-  __shared__ float red[kRowsThreads / 32][kRowsPerCta * MR];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int o0 = blockIdx.x * kRowsPerCta;
+template <int MR, int R>
+__global__ void __launch_bounds__(kRowsWarps * 32) linear_rows_kernel(const float* __restrict__ x,
+                                                                      const __half* __restrict__ w,
+                                                                      float* __restrict__ y, int m,
+                                                                      int in_f, int out_f) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o0 = (blockIdx.x * kRowsWarps + warp) * R;
+  if (o0 >= out_f) return;
   const int n_chunks = in_f / 8;
-  float acc[kRowsPerCta][MR];
+  float acc[R][MR];
 #pragma unroll
-  for (int r = 0; r < kRowsPerCta; r++)
+  for (int r = 0; r < R; r++)
 #pragma unroll
     for (int i = 0; i < MR; i++) acc[r][i] = 0.f;
 
-  for (int c0 = tid; c0 < n_chunks; c0 += kRowsThreads * kRowsUnroll) {
-    uint4 wv[kRowsUnroll][kRowsPerCta];
+  for (int c0 = lane; c0 < n_chunks; c0 += 32 * kRowsBatch) {
+    uint4 wv[kRowsBatch][R];
 #pragma unroll
-    for (int u = 0; u < kRowsUnroll; u++) {
-      const int c = c0 + u * kRowsThreads;
+    for (int u = 0; u < kRowsBatch; u++) {
+      const int c = c0 + 32 * u;
 #pragma unroll
-      for (int r = 0; r < kRowsPerCta; r++) {
-        const int o = o0 + r;
-        wv[u][r] = (c < n_chunks && o < out_f)
-                       ? ld_stream_u4(w + (int64_t)o * in_f + (int64_t)c * 8)
+      for (int r = 0; r < R; r++)
+        wv[u][r] = (c < n_chunks && o0 + r < out_f)
+                       ? ld_stream_u4(w + (int64_t)(o0 + r) * in_f + (int64_t)c * 8)
                        : make_uint4(0, 0, 0, 0);
-      }
     }
 #pragma unroll
-    for (int u = 0; u < kRowsUnroll; u++) {
-      const int c = c0 + u * kRowsThreads;
+    for (int u = 0; u < kRowsBatch; u++) {
+      const int c = c0 + 32 * u;
       if (c >= n_chunks) break;
-      float wf[kRowsPerCta][8];
+      float wf[R][8];
 #pragma unroll
-      for (int r = 0; r < kRowsPerCta; r++) {
+      for (int r = 0; r < R; r++) {
         const __half2* h2 = reinterpret_cast<const __half2*>(&wv[u][r]);
 #pragma unroll
         for (int e = 0; e < 4; e++) {
@@ -88,27 +88,19 @@ __global__ void __launch_bounds__(kRowsThreads) linear_rows_kernel(const float* 
         const float4 xa = __ldg(xp), xb = __ldg(xp + 1);
         const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
-        for (int r = 0; r < kRowsPerCta; r++)
+        for (int r = 0; r < R; r++)
 #pragma unroll
           for (int e = 0; e < 8; e++) acc[r][i] = fmaf(xv[e], wf[r][e], acc[r][i]);
       }
     }
   }
 #pragma unroll
-  for (int r = 0; r < kRowsPerCta; r++)
+  for (int r = 0; r < R; r++)
 #pragma unroll
     for (int i = 0; i < MR; i++) {
       const float v = warp_sum(acc[r][i]);
-      if (lane == 0) red[warp][r * MR + i] = v;
+      if (lane == 0 && i < m && o0 + r < out_f) y[(int64_t)i * out_f + o0 + r] = v;
     }
-  __syncthreads();
-  if (tid < kRowsPerCta * MR) {
-    const int r = tid / MR, i = tid % MR;
-    float v = 0.f;
-#pragma unroll
-    for (int wi = 0; wi < kRowsThreads / 32; wi++) v += red[wi][tid];
-    if (i < m && o0 + r < out_f) y[(int64_t)i * out_f + o0 + r] = v;
-  }
 }
 
 // ---------------------------------------------------------------- any shape
@@ -338,15 +330,23 @@ cudaError_t launch_linear(const float* x, const void* w, float* y, int64_t m, in
     return cudaGetLastError();
   }
   if (path == LinearPath::kRows) {
-    const unsigned grid = (unsigned)((out_f + kRowsPerCta - 1) / kRowsPerCta);
-    if (m == 1)
-      linear_rows_kernel<1><<<grid, kRowsThreads, 0, st>>>(x, wh, y, (int)m, (int)in_f, (int)out_f);
-    else if (m == 2)
-      linear_rows_kernel<2><<<grid, kRowsThreads, 0, st>>>(x, wh, y, (int)m, (int)in_f, (int)out_f);
-    else if (m <= 4)
-      linear_rows_kernel<4><<<grid, kRowsThreads, 0, st>>>(x, wh, y, (int)m, (int)in_f, (int)out_f);
-    else
-      linear_rows_kernel<8><<<grid, kRowsThreads, 0, st>>>(x, wh, y, (int)m, (int)in_f, (int)out_f);
+    // 4 rows per warp when that still gives two CTAs per SM, else 1
+    const bool wide = out_f >= (int64_t)2 * 148 * kRowsWarps * 4;
+    const int rows_per_cta = kRowsWarps * (wide ? 4 : 1);
+    const unsigned grid = (unsigned)((out_f + rows_per_cta - 1) / rows_per_cta);
+    const int mi = (int)m, ki = (int)in_f, ni = (int)out_f;
+    constexpr int T = kRowsWarps * 32;
+    if (wide) {
+      if (m == 1) linear_rows_kernel<1, 4><<<grid, T, 0, st>>>(x, wh, y, mi, ki, ni);
+      else if (m == 2) linear_rows_kernel<2, 4><<<grid, T, 0, st>>>(x, wh, y, mi, ki, ni);
+      else if (m <= 4) linear_rows_kernel<4, 4><<<grid, T, 0, st>>>(x, wh, y, mi, ki, ni);
+      else linear_rows_kernel<8, 4><<<grid, T, 0, st>>>(x, wh, y, mi, ki, ni);
+    } else {
+      if (m == 1) linear_rows_kernel<1, 1><<<grid, T, 0, st>>>(x, wh, y, mi, ki, ni);
+      else if (m == 2) linear_rows_kernel<2, 1><<<grid, T, 0, st>>>(x, wh, y, mi, ki, ni);
+      else if (m <= 4) linear_rows_kernel<4, 1><<<grid, T, 0, st>>>(x, wh, y, mi, ki, ni);
+      else linear_rows_kernel<8, 1><<<grid, T, 0, st>>>(x, wh, y, mi, ki, ni);
+    }
     return cudaGetLastError();
   }
   using C = LinCfg;
