@@ -234,14 +234,20 @@ class PrefillWork:
     """Head-sharded fused prefill (eb_attention_prefill) + all-gather + concat."""
 
     def __init__(self, name, S, H, Hkv, hd, theta, dt, in_scale=1.0, scale=None, qk_norm=False,
-                 v_norm=False, rope_angles=None, seed=0):
+                 v_norm=False, rope_angles=None, seed=0, window=0):
         self.name, self.S, self.H, self.Hkv, self.hd = name, S, H, Hkv, hd
+        self.window = window
         self.theta, self.dt, self.in_scale, self.seed = theta, dt, in_scale, seed
         self.scale = scale if scale is not None else hd ** -0.5
         self.qk_norm, self.v_norm, self.rope_angles = qk_norm, v_norm, rope_angles
         self.graph_reps = 20 if S <= 1024 else 0  # launch-bound sizes replay a CUDA graph
 
     def flops(self) -> float:
+        # 4 FLOP per (query row, visible key, dim): QK^T and PV, 2 per MAC
+        if self.window and self.window < self.S:
+            W, S = self.window, self.S
+            keys = W * (W + 1) / 2 + (S - W) * W  # rows i < W see i + 1 keys, later rows W
+            return 4.0 * self.hd * self.H * keys
         return 2.0 * self.hd * self.H * self.S * (self.S + 1)
 
     def describe(self, world):
@@ -249,6 +255,7 @@ class PrefillWork:
                 "n_kv_heads": self.Hkv, "head_dim": self.hd, "rope_theta": self.theta,
                 "scale": round(self.scale, 6), "qk_norm": self.qk_norm, "v_norm": self.v_norm,
                 "rope_angles": self.rope_angles or self.hd // 2, "batch": 1,
+                "window": self.window or None,
                 "parallelism": f"heads/{world}" if world > 1 else "1 GPU",
                 "head_concat": self._concat_desc(world)}
 
@@ -293,7 +300,8 @@ class PrefillWork:
             vw = torch.ones(hd, device="cuda")
         self._keep = (qw, kw, vw)
         self.desc = eb.make_desc(self.Hl, self.Hkvl, hd, S, dtype_qkv=self.dt,
-                                 dtype_cache=self.dt, dtype_out=self.dt, scale=self.scale)
+                                 dtype_cache=self.dt, dtype_out=self.dt, scale=self.scale,
+                                 window=self.window)
         self.layer = eb.make_layer(qw, kw, vw, self.cos, self.sin)
         nb = eb.attention_prefill_workspace_bytes(self.desc, S)
         self.ws = eb.alloc_workspace(nb) if nb else None
@@ -346,7 +354,7 @@ class PrefillWork:
                                          self.o, self.ws)
 
     def kernel_units(self):
-        return 2.0 * self.hd * self.Hl * self.S * (self.S + 1)  # this rank's FLOP per launch
+        return self.flops() * self.Hl / self.H  # this rank's FLOP per launch
 
     # e2e through the public API with host buffers
     def setup_e2e(self):
@@ -355,6 +363,27 @@ class PrefillWork:
         self.hk = self.k.cpu().pin_memory()
         self.hv = self.v.cpu().pin_memory()
         self.hout = torch.empty(self.full.shape, dtype=self.full.dtype).pin_memory()
+
+    def e2e_pipelined(self, steps, unit, total_units):
+        """One GPU: the e2e loop pipelined over two slots (time_e2e_pipelined)."""
+        import torch
+        self.setup_e2e()
+        second = [torch.empty_like(t) for t in (self.q, self.k, self.v, self.o)]
+        slots = [([self.q, self.k, self.v], self.o, self.hout),
+                 (second[:3], second[3], torch.empty_like(self.hout).pin_memory())]
+        api = self.eb
+
+        def run(a):
+            q, k, v, o = (self.q, self.k, self.v, self.o) if a == 0 else second
+            api.attention_prefill(self.desc, self.layer, self.S, q, k, v, self.kc, self.vc, o,
+                                  self.ws)
+        ems = time_e2e_pipelined(slots, [self.hq, self.hk, self.hv], run, steps, 2)
+        return {"value": total_units / (ems / steps * 1e-3) / 1e12, "unit": unit,
+                "h2d_bytes_per_step": int(self.bytes_in),
+                "d2h_bytes_per_step": int(self.hout.numel() * self.hout.element_size()),
+                "note": "pinned host q/k/v in, o out every step through eb_attention_prefill; "
+                        "steps pipelined over two slots (upload, compute, download on "
+                        "separate streams)"}
 
     def step_e2e(self, rank):
         self.q.copy_(self.hq, non_blocking=True)
@@ -554,16 +583,21 @@ class LinearWork:
     def e2e(self, rank, world, steps, unit):
         import torch
         hx = self.x.cpu().pin_memory()
-        hy = torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
+        x2, y2 = torch.empty_like(self.x), torch.empty_like(self.y)
+        slots = [([self.x], self.y, torch.empty(self.y.shape).pin_memory()),
+                 ([x2], y2, torch.empty(self.y.shape).pin_memory())]
+        eb = self.eb
 
-        def st():
-            self.x.copy_(hx, non_blocking=True)
-            self.step()
-            hy.copy_(self.y, non_blocking=True)
-        ems, _ = time_steps(st, steps, 2, world)
+        def run(a):
+            xs, ys = (self.x, self.y) if a == 0 else (x2, y2)
+            eb.linear_f16w(xs, self.w, ys, self.m, self.k, self.n, self.ws)
+        ems = max_over_ranks(time_e2e_pipelined(slots, [hx], run, steps, 2), world)
         units = self.flops() / 1e12 if self.bound == "tensor" else self.bytes_total() / 1e9
         return {"value": units / (ems / steps * 1e-3), "unit": unit,
-                "h2d_bytes_per_step": int(hx.numel() * 4), "d2h_bytes_per_step": int(hy.numel() * 4)}
+                "h2d_bytes_per_step": int(hx.numel() * 4),
+                "d2h_bytes_per_step": int(self.y.numel() * 4),
+                "note": "pinned host x in, y out every step; steps pipelined over two slots "
+                        "(upload, compute, download on separate streams)"}
 
 
 def cpu_baseline_linear(w: LinearWork, threads: int | None = None, target_s: float = 8.0):
@@ -597,6 +631,9 @@ def make_workload(name, batch=None):
     if name == "cfg3":
         return PrefillWork("cfg3 causal GQA prefill S8192 H32 Hkv8 hd128 f16 (Llama-3-8B layer)",
                            8192, 32, 8, 128, 5e5, 1, in_scale=0.5, seed=3)
+    if name == "cfg3w":
+        return PrefillWork("cfg3w config 3 with a 1024-row sliding window (S8192 H32 Hkv8 hd128 "
+                           "f16)", 8192, 32, 8, 128, 5e5, 1, in_scale=0.5, seed=3, window=1024)
     if name == "cfg4":
         return PrefillWork("cfg4 Gemma-style prefill S4096 H8 Hkv4 hd256 f32 scale 1.0 "
                            "QK-norm V-norm partial rotary 32/128", 4096, 8, 4, 256, 1e6, 0,
@@ -651,6 +688,59 @@ def time_steps(fn, steps, warmup, world, stream=None, min_warm_s=0.0):
     return max_over_ranks(ms, world), (t_wall0, t_wall1)
 
 
+def time_e2e_pipelined(slots, h_inputs, run, steps, warmup):
+    """Device time (CUDA events) of `steps` end-to-end steps: every step copies
+    its inputs in from pinned host memory, runs the public API call and copies
+    its result back to pinned host memory. Steps alternate between two device
+    slots on three streams (upload, compute, download), so step i+1's upload
+    and step i-1's download overlap step i's compute, as a serving loop
+    would. slots[a] = (device inputs, device output, pinned host output);
+    run(a) issues slot a's computation on the current stream."""
+    import torch
+    s_in, s_cmp, s_out = (torch.cuda.Stream() for _ in range(3))
+    ev_in, ev_cmp, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+    n = [0]
+
+    def one():
+        i = n[0]
+        a = i & 1
+        d_in, d_out, h_out = slots[a]
+        if i >= 2:
+            s_in.wait_event(ev_cmp[a])   # step i-2's compute has read this slot's inputs
+        with torch.cuda.stream(s_in):
+            for d, h in zip(d_in, h_inputs):
+                d.copy_(h, non_blocking=True)
+        ev_in[a].record(s_in)
+        s_cmp.wait_event(ev_in[a])
+        if i >= 2:
+            s_cmp.wait_event(ev_out[a])  # step i-2's download has read this slot's output
+        with torch.cuda.stream(s_cmp):
+            run(a)
+        ev_cmp[a].record(s_cmp)
+        s_out.wait_event(ev_cmp[a])
+        with torch.cuda.stream(s_out):
+            h_out.copy_(d_out, non_blocking=True)
+        ev_out[a].record(s_out)
+        n[0] = i + 1
+        return a
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    cur = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for st in (s_in, s_cmp, s_out):
+        st.wait_event(e0)
+    a = 0
+    for _ in range(steps):
+        a = one()
+    cur.wait_event(ev_out[a])  # the download stream is in order: its last copy ends the run
+    e1.record(cur)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
 _CPU_INPUTS = {}
 
 
@@ -678,9 +768,11 @@ def cpu_baseline_prefill(w: PrefillWork, target_s: float = 12.0, threads: int | 
     while True:
         r0 = S - rows_n
         t0 = time.perf_counter()
-        orc.attn_prefill_part(q, k, v, H, Hkv, S, hd, w.scale, (r0, S), (0, nh), threads)
+        W = w.window if w.window and w.window < S else S
+        orc.attn_prefill_part(q, k, v, H, Hkv, S, hd, w.scale, (r0, S), (0, nh), threads,
+                              window=W if W < S else 0)
         dt = time.perf_counter() - t0
-        flop = sum(4.0 * hd * (i + 1) for i in range(r0, S)) * nh
+        flop = sum(4.0 * hd * min(i + 1, W) for i in range(r0, S)) * nh
         if sample or dt >= target_s / 2 or (rows_n >= S and nh >= H):
             break
         grow = max(2.0, (target_s / 1.5) / max(dt, 1e-3))
@@ -810,7 +902,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                     help="N>1 head-concat exchange: fused into the attention kernel "
                          "(default) or NCCL all-gather + concat")
@@ -863,6 +955,8 @@ def main():
     e2e = None
     if hasattr(w, "e2e"):
         e2e = w.e2e(rank, world, args.e2e_steps, unit)
+    elif is_prefill and world == 1:
+        e2e = w.e2e_pipelined(args.e2e_steps, unit, total_units)
     elif is_prefill:
         w.setup_e2e()
         bi = bo = 0
