@@ -788,6 +788,13 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* q16, con
   const double per_sm = (double)a.H * n_qt * (n_qt + 1) / 2 / (n_sm > 0 ? n_sm : 148);
   const bool pair = ((a.H / a.Hkv) % 2) == 0 &&
                     std::max(2 * n_qt, per_sm) <= std::max(n_qt, per_sm) / 0.87;
+  // A contiguous [S][H][hd] output is a one-destination gather: its tiles are
+  // staged in shared memory and leave by TMA store, 1.4% faster on config 3
+  // than per-thread 16-byte stores (bit-identical). Strided outputs keep the
+  // per-thread stores.
+  uint64_t self_dst = reinterpret_cast<uint64_t>(a.o);
+  GatherSpec self_g{1, 0, a.H, &self_dst};
+  if (!g && a.o && a.o_stride == (int64_t)a.H * hd && (self_dst & 15) == 0) g = &self_g;
   if (split) {
     switch (hd) {
       case 64:
