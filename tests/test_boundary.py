@@ -60,6 +60,13 @@ def test_host_validation_precedes_device_work(eb):
                                   0, None) == 1
     assert L.eb_attention_decode(ctypes.byref(d), ctypes.byref(lay), 4096, 1, 1, 1, 1, 1, 1, None,
                                  0, None) == 1
+    neg = eb.make_desc(16, 8, 128, 4096, window=-1)  # a window is a row count
+    assert L.eb_attention_prefill(ctypes.byref(neg), ctypes.byref(lay), 4, 1, 1, 1, 1, 1, 1, None,
+                                  0, None) == 1
+    # linear_f16w: shapes are checked before anything else; m = 0 is a no-op
+    assert L.eb_linear_f16w(16, 16, 16, -1, 64, 64, None, 0, None) == 1
+    assert L.eb_linear_f16w(16, 16, 16, 4, 0, 64, None, 0, None) == 1
+    assert L.eb_linear_f16w(16, 16, 16, 0, 64, 64, None, 0, None) == 0
 
 
 def test_no_device_is_reported_not_faked(eb):
@@ -69,6 +76,29 @@ def test_no_device_is_reported_not_faked(eb):
     L = eb.lib()
     # valid arguments, no GPU: the call must refuse, never compute elsewhere
     assert L.eb_rope(1, 1, 1, 1, 1, 1, 8, 0, None) == 5
+    assert L.eb_linear_f16w(16, 16, 16, 4, 64, 64, None, 0, None) == 5
+
+
+def test_linear_workspace_sizes(eb):
+    # m <= 8 streams the weights (no workspace); m > 8 splits x into two f16
+    # planes, each rounded up to 256 bytes; other shapes take the scalar kernel
+    assert eb.linear_f16w_workspace_bytes(8, 1024, 4096) == 0
+    assert eb.linear_f16w_workspace_bytes(9, 1024, 4096) == 2 * 9 * 1024 * 2
+    assert eb.linear_f16w_workspace_bytes(300, 200, 260) == 2 * ((300 * 200 * 2 + 255) // 256 * 256)
+    assert eb.linear_f16w_workspace_bytes(100, 33, 64) == 0   # k not a multiple of 8
+    assert eb.linear_f16w_workspace_bytes(100, 64, 62) == 0   # out not a multiple of 4
+    assert eb.linear_f16w_workspace_bytes(0, 64, 64) == 0
+
+
+def test_window_caps_decode_workspace(eb):
+    """A sliding-window layer's decode never attends more than `window` rows:
+    its workspace is the full-context workspace of a window-row context."""
+    full = eb.make_desc(16, 8, 128, 1 << 17)
+    win = eb.make_desc(16, 8, 128, 1 << 17, window=1024)
+    assert (eb.attention_decode_workspace_bytes(win, 1, (1 << 17) - 1)
+            == eb.attention_decode_workspace_bytes(full, 1, 1023))
+    assert (eb.attention_decode_workspace_bytes(win, 1, 500)
+            == eb.attention_decode_workspace_bytes(full, 1, 500))
 
 
 def test_workspace_sizes(eb):
