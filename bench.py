@@ -601,9 +601,11 @@ class LinearWork:
 
 
 def cpu_baseline_linear(w: LinearWork, threads: int | None = None, target_s: float = 8.0):
-    """Oracle cpu_linear (single thread, the reference's loop order) over a
-    bounded sample of output columns, scaled to the workload's unit."""
+    """Oracle cpu_linear (the reference's loop order) on all host threads,
+    parallel over output features, over a bounded sample of output columns,
+    scaled to the workload's unit."""
     from oracle import oracle as orc
+    threads = threads or len(os.sched_getaffinity(0))
     rng = np.random.default_rng(0)
     m = min(w.m, 8)
     x = rng.standard_normal((m, w.k)).astype(np.float32)
@@ -611,17 +613,17 @@ def cpu_baseline_linear(w: LinearWork, threads: int | None = None, target_s: flo
     while True:
         wt = (rng.standard_normal((n, w.k)) * 0.02).astype(np.float16).astype(np.float32)
         t0 = time.perf_counter()
-        orc.linear(x, wt, m, w.k, n)
+        orc.linear_threaded(x, wt, m, w.k, n, threads)
         dt = time.perf_counter() - t0
         if dt >= target_s / 4 or n >= w.n:
             break
         n = min(w.n, int(n * max(2.0, target_s / 2 / max(dt, 1e-4))))
     flop, nbytes = 2.0 * m * n * w.k, 2.0 * n * w.k
     value = flop / dt / 1e12 if w.bound == "tensor" else nbytes / dt / 1e9
-    return {"value": value, "unit": "TFLOP/s" if w.bound == "tensor" else "GB/s", "cores": 1,
-            "kind": "port",
+    return {"value": value, "unit": "TFLOP/s" if w.bound == "tensor" else "GB/s",
+            "cores": threads, "kind": "port",
             "sample": f"oracle cpu_linear, {m} rows x {n} of {w.n} outputs, k={w.k} "
-                      f"({dt:.2f} s, f32, gcc -O3 -ffp-contract=off, 1 thread)"}
+                      f"({dt:.2f} s, f32, gcc -O3 -ffp-contract=off, {threads} threads)"}
 
 
 def make_workload(name, batch=None):
@@ -827,7 +829,7 @@ def run_reference(args):
         elif isinstance(w, BatchedDecodeWork):
             b = cpu_baseline_decode(w, threads=threads, n_seq=2)
         elif isinstance(w, LinearWork):
-            b = cpu_baseline_linear(w, target_s=per_step)
+            b = cpu_baseline_linear(w, threads=threads, target_s=per_step)
         else:
             raise SystemExit("--impl reference supports cfg1, cfg3, cfg4, cfg5, proj3, projd")
         if i >= args.warmup:

@@ -183,6 +183,41 @@ void orc_linear(const float* x, const float* w, float* y, size_t m, size_t in_f,
     }
 }
 
+typedef struct {
+  const float *x, *w;
+  float* y;
+  size_t m, in_f, out_f;
+  atomic_size_t next;
+} linear_job;
+
+static void* linear_worker(void* arg) {
+  linear_job* jb = (linear_job*)arg;
+  for (;;) {
+    /* one output row o (all m inputs) per task, same inner loop as orc_linear */
+    size_t o = atomic_fetch_add(&jb->next, 1);
+    if (o >= jb->out_f) break;
+    for (size_t i = 0; i < jb->m; i++) {
+      float acc = 0.0f;
+      for (size_t k = 0; k < jb->in_f; k++) acc += jb->x[i * jb->in_f + k] * jb->w[o * jb->in_f + k];
+      jb->y[i * jb->out_f + o] = acc;
+    }
+  }
+  return NULL;
+}
+
+void orc_linear_threaded(const float* x, const float* w, float* y, size_t m, size_t in_f,
+                         size_t out_f, int nthreads) {
+  linear_job jb;
+  jb.x = x; jb.w = w; jb.y = y; jb.m = m; jb.in_f = in_f; jb.out_f = out_f;
+  atomic_init(&jb.next, 0);
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads == 1) { linear_worker(&jb); return; }
+  pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)nthreads);
+  for (int t = 0; t < nthreads; t++) pthread_create(&th[t], NULL, linear_worker, &jb);
+  for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
+  free(th);
+}
+
 /* One (query row, head) of the two-pass attention in testutil.rs:142-169.
  * `scores` has room for n_keys floats. */
 static void attn_row(const float* qrow, const float* k, const float* v, float* orow,

@@ -68,6 +68,12 @@ void orc_kv_write(float* cache, const float* src, size_t hkv, size_t count, size
  * reference of linear_f16w (matmul.rs:128-149) with f16-rounded w. */
 void orc_linear(const float* x, const float* w, float* y, size_t m, size_t in_f, size_t out_f);
 
+/* orc_linear spread over `nthreads` POSIX threads by output feature, with the
+ * identical inner loop (bit-identical results). Used by the timed CPU
+ * baseline. */
+void orc_linear_threaded(const float* x, const float* w, float* y, size_t m, size_t in_f,
+                         size_t out_f, int nthreads);
+
 /* Causal GQA attention, seq-major: q [s,h,hd], k/v [s,hkv,hd] -> o [s,h,hd].
  * crates/eyebrowse-kernels/src/testutil.rs:130-172 (two-pass softmax, f32 dot
  * accumulated over d in order, then *= scale). */

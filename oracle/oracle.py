@@ -51,6 +51,7 @@ def lib():
         L.orc_rope_tables.argtypes = [_fp, _fp, _sz, _sz, _sz, ctypes.c_float]
         L.orc_kv_write.argtypes = [_fp, _fp, _sz, _sz, _sz, _sz, _sz]
         L.orc_linear.argtypes = [_fp, _fp, _fp, _sz, _sz, _sz]
+        L.orc_linear_threaded.argtypes = [_fp, _fp, _fp, _sz, _sz, _sz, ctypes.c_int]
         L.orc_attn_prefill.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz, ctypes.c_float]
         L.orc_attn_prefill_window.argtypes = [_fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz,
                                               ctypes.c_float, _sz]
@@ -158,6 +159,14 @@ def linear(x, w, m: int, in_f: int, out_f: int) -> np.ndarray:
     x, w = _f32(x), _f32(w)
     y = np.empty(m * out_f, np.float32)
     lib().orc_linear(_p(x), _p(w), _p(y), m, in_f, out_f)
+    return y
+
+
+def linear_threaded(x, w, m: int, in_f: int, out_f: int, nthreads: int) -> np.ndarray:
+    """linear() over `nthreads` threads by output feature (bit-identical)."""
+    x, w = _f32(x), _f32(w)
+    y = np.empty(m * out_f, np.float32)
+    lib().orc_linear_threaded(_p(x), _p(w), _p(y), m, in_f, out_f, nthreads)
     return y
 
 

@@ -139,6 +139,15 @@ def test_linear_ramp(orc):
     assert got[0] == acc
 
 
+def test_linear_threaded_is_bit_identical(orc):
+    rng = np.random.default_rng(5)
+    m, in_f, out_f = 3, 200, 77
+    x = rng.standard_normal(m * in_f).astype(np.float32)
+    w = orc.round_f16(rng.standard_normal(out_f * in_f).astype(np.float32))
+    assert np.array_equal(orc.linear(x, w, m, in_f, out_f),
+                          orc.linear_threaded(x, w, m, in_f, out_f, 4))
+
+
 def test_attn_prefill_ramp(orc):
     # crates/eyebrowse-kernels/src/attention.rs:174-202 inputs
     h, hkv, s, hd = 2, 1, 5, 8
