@@ -148,6 +148,28 @@ def test_linear_threaded_is_bit_identical(orc):
                           orc.linear_threaded(x, w, m, in_f, out_f, 4))
 
 
+def test_windowed_decode_batched_equals_single(orc):
+    """orc_attn_decode_batched with a window = orc_attn_decode_window per
+    sequence = the full decode over the window's rows only."""
+    rng = np.random.default_rng(9)
+    h, hkv, hd, ms, window = 4, 2, 16, 64, 10
+    pos = np.array([3, 9, 10, 40, 63], np.int32)
+    B = pos.size
+    kc = rng.standard_normal((B, ms, hkv, hd)).astype(np.float32)
+    vc = rng.standard_normal((B, ms, hkv, hd)).astype(np.float32)
+    q = rng.standard_normal((B, h, hd)).astype(np.float32)
+    got = orc.attn_decode_batched(q, kc, vc, pos, h, hkv, hd, ms, ms * hkv * hd, 0.25,
+                                  nthreads=2, window=window).reshape(B, h * hd)
+    for b, p in enumerate(pos):
+        one = orc.attn_decode(q[b], kc[b], vc[b], h, hkv, int(p), hd, ms, 0.25, window=window)
+        assert np.array_equal(got[b], one)
+        lo = max(0, int(p) - window + 1)
+        # the same rows moved to the front of a cache: a plain full decode
+        sub = orc.attn_decode(q[b], kc[b, lo:p + 1], vc[b, lo:p + 1], h, hkv, int(p) - lo, hd,
+                              ms, 0.25)
+        assert np.array_equal(one, sub)
+
+
 def test_attn_prefill_ramp(orc):
     # crates/eyebrowse-kernels/src/attention.rs:174-202 inputs
     h, hkv, s, hd = 2, 1, 5, 8
