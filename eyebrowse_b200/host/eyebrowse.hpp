@@ -266,6 +266,8 @@ struct Linear {
 // (GQA heads, optional per-head q/k/v RMSNorm weights, scale), prefill over
 // positions 0..seq and decode at pos, both writing the layer's cache.
 struct Attention {
+  // attention.rs:11-14 (projections; needed by forward() only)
+  std::optional<Linear> q_proj, k_proj, v_proj, o_proj;
   std::optional<Tensor> q_norm, k_norm, v_norm;  // [head_dim] weights
   size_t n_heads = 0, n_kv_heads = 0, head_dim = 0;
   float scale = 0.f, eps = 1e-6f;
@@ -296,6 +298,23 @@ struct Attention {
     l.rope_cos = static_cast<const float*>(rope.cos.ptr());
     l.rope_sin = static_cast<const float*>(rope.sin.ptr());
     return l;
+  }
+  // attention.rs:30-45: x [rows, hidden] at positions base_pos.. -> [rows, hidden].
+  // A fresh multi-row prompt (base_pos 0, rows > 1) takes the prefill path,
+  // anything else one decode step (one row), as in the reference.
+  Tensor forward(Recorder& rec, const Tensor& x, const Rope& rope, KvCache& kv, size_t layer_idx,
+                 size_t rows, size_t base_pos) const {
+    if (!q_proj || !k_proj || !v_proj || !o_proj)
+      throw Error("Attention::forward: projections not set", EB_ERR_INVALID_ARGUMENT);
+    const bool is_prefill = base_pos == 0 && rows > 1;
+    if (!is_prefill && rows != 1)
+      throw Error("Attention::forward: a decode step takes one row", EB_ERR_INVALID_ARGUMENT);
+    const Tensor q = q_proj->forward(rec, x, rows);
+    const Tensor k = k_proj->forward(rec, x, rows);
+    const Tensor v = v_proj->forward(rec, x, rows);
+    const Tensor o = is_prefill ? prefill(rec, q, k, v, rope, kv, layer_idx, rows)
+                                : decode(rec, q, k, v, rope, kv, layer_idx, base_pos);
+    return o_proj->forward(rec, o, rows);
   }
   // q [seq, n_heads*hd], k/v [seq, n_kv_heads*hd] -> o [seq, n_heads*hd]
   Tensor prefill(Recorder& rec, const Tensor& q, const Tensor& k, const Tensor& v,

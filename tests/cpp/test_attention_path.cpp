@@ -336,6 +336,86 @@ void linear_forward_decode_and_prefill() {
   }
 }
 
+// crates/eyebrowse-nn/src/attention.rs:30-185 with its projections:
+// Attention::forward over a prompt (prefill), then one token (decode),
+// against cpu_linear + the oracle attention on the same f16 weights.
+void attention_forward_with_projections() {
+  const size_t hidden = 256, n_heads = 4, n_kv_heads = 2, hd = 64, seq = 40, max_seq = 48;
+  const size_t q_dim = n_heads * hd, kv_dim = n_kv_heads * hd;
+  auto weight = [](size_t out_f, size_t in_f, uint64_t seed) {
+    auto w = prng(out_f * in_f, seed);
+    for (auto& x : w) x *= 0.05f;
+    orc_round_f16(w.data(), w.size());  // the f16 values the device holds
+    return w;
+  };
+  auto linear = [](const std::vector<float>& w, size_t in_f, size_t out_f) {
+    nn::Linear l;
+    l.w = Tensor::from_f16({out_f, in_f}, w);
+    l.in_f = in_f;
+    l.out_f = out_f;
+    return l;
+  };
+  auto wq = weight(q_dim, hidden, 61), wk = weight(kv_dim, hidden, 62);
+  auto wv = weight(kv_dim, hidden, 63), wo = weight(hidden, q_dim, 64);
+  auto qn = prng(hd, 65), kn = prng(hd, 66);
+  for (auto& x : qn) x = 1.f + 0.1f * x;
+  for (auto& x : kn) x = 1.f + 0.1f * x;
+  nn::Attention attn;
+  attn.q_proj = linear(wq, hidden, q_dim);
+  attn.k_proj = linear(wk, hidden, kv_dim);
+  attn.v_proj = linear(wv, hidden, kv_dim);
+  attn.o_proj = linear(wo, q_dim, hidden);
+  attn.q_norm = Tensor::from_f32({hd}, qn);
+  attn.k_norm = Tensor::from_f32({hd}, kn);
+  attn.n_heads = n_heads;
+  attn.n_kv_heads = n_kv_heads;
+  attn.head_dim = hd;
+  attn.scale = 1.0f / std::sqrt((float)hd);
+  auto rope = nn::Rope::build(max_seq, hd, 1e6f);
+  auto kv = nn::KvCache::create(1, max_seq, n_kv_heads, hd);
+  auto cos = rope.cos.to_f32(), sin = rope.sin.to_f32();
+  std::vector<float> kc(max_seq * kv_dim, 0.f), vc(max_seq * kv_dim, 0.f);
+  Recorder rec;
+
+  auto x = prng(seq * hidden, 67);
+  auto y = attn.forward(rec, Tensor::from_f32({seq, hidden}, x), rope, kv, 0, seq, 0);
+  rec.submit();
+  auto got = y.to_f32();
+  std::vector<float> q(seq * q_dim), k(seq * kv_dim), v(seq * kv_dim), o(seq * q_dim);
+  std::vector<float> want(seq * hidden);
+  orc_linear(x.data(), wq.data(), q.data(), seq, hidden, q_dim);
+  orc_linear(x.data(), wk.data(), k.data(), seq, hidden, kv_dim);
+  orc_linear(x.data(), wv.data(), v.data(), seq, hidden, kv_dim);
+  orc_attention_prefill(q.data(), k.data(), v.data(), qn.data(), kn.data(), nullptr, 1e-6f,
+                        cos.data(), sin.data(), kc.data(), vc.data(), o.data(), seq, n_heads,
+                        n_kv_heads, hd, max_seq, attn.scale, ORC_F32, ORC_F32, 0);
+  orc_linear(o.data(), wo.data(), want.data(), seq, q_dim, hidden);
+  CHECK(max_abs(got, want) <= 2e-3f && rel_l2(got, want) <= 1e-3f, "prefill forward");
+
+  auto xd = prng(hidden, 68);
+  auto yd = attn.forward(rec, Tensor::from_f32({1, hidden}, xd), rope, kv, 0, 1, seq);
+  rec.submit();
+  auto got_d = yd.to_f32();
+  std::vector<float> qd(q_dim), kd(kv_dim), vd(kv_dim), od(q_dim), want_d(hidden);
+  orc_linear(xd.data(), wq.data(), qd.data(), 1, hidden, q_dim);
+  orc_linear(xd.data(), wk.data(), kd.data(), 1, hidden, kv_dim);
+  orc_linear(xd.data(), wv.data(), vd.data(), 1, hidden, kv_dim);
+  orc_attention_decode(qd.data(), kd.data(), vd.data(), qn.data(), kn.data(), nullptr, 1e-6f,
+                       cos.data(), sin.data(), kc.data(), vc.data(), od.data(), seq, n_heads,
+                       n_kv_heads, hd, max_seq, attn.scale, ORC_F32, 0);
+  orc_linear(od.data(), wo.data(), want_d.data(), 1, q_dim, hidden);
+  CHECK(max_abs(got_d, want_d) <= 2e-3f && rel_l2(got_d, want_d) <= 1e-3f, "decode forward");
+
+  // a decode step takes one row (the reference's decode reads one)
+  bool threw = false;
+  try {
+    attn.forward(rec, Tensor::from_f32({2, hidden}, prng(2 * hidden, 69)), rope, kv, 0, 2, seq);
+  } catch (const Error& e) {
+    threw = e.status == EB_ERR_INVALID_ARGUMENT;
+  }
+  CHECK(threw, "two rows at base_pos > 0 are refused");
+}
+
 // Where the reference panics on a bad shape, the mirror throws Error.
 void invalid_shapes_throw() {
   auto x = Tensor::zeros({64});
@@ -370,6 +450,7 @@ int main(int argc, char** argv) {
       {"sliding_window_prefill_and_decode", sliding_window_prefill_and_decode},
       {"linear_f16w_matches_cpu", linear_f16w_matches_cpu},
       {"linear_forward_decode_and_prefill", linear_forward_decode_and_prefill},
+      {"attention_forward_with_projections", attention_forward_with_projections},
       {"invalid_shapes_throw", invalid_shapes_throw},
   };
   if (argc > 1 && std::string(argv[1]) == "--list") {

@@ -15,7 +15,8 @@ NAMES = ["attn_prefill_matches_cpu", "attn_decode_matches_cpu", "rope_matches_cp
          "rmsnorm_matches_cpu", "kv_write_places_rows", "rope_build_tables",
          "prefill_decode_consistency", "attn_prefill_tensor_core_hd128",
          "attention_decode_long_context_hd128", "sliding_window_prefill_and_decode",
-         "linear_f16w_matches_cpu", "linear_forward_decode_and_prefill", "invalid_shapes_throw"]
+         "linear_f16w_matches_cpu", "linear_forward_decode_and_prefill",
+         "attention_forward_with_projections", "invalid_shapes_throw"]
 
 
 def _build():
