@@ -20,17 +20,23 @@ static unsigned* error_word_ptr() {
   static unsigned* ptrs[64] = {};
   static std::mutex mu;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
   std::lock_guard<std::mutex> lock(mu);
   if (!ptrs[dev]) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_eb_error_word) != cudaSuccess) return nullptr;
+    if (cudaGetSymbolAddress(&p, g_eb_error_word) != cudaSuccess) {
+      cudaGetLastError();  // clear the failed lookup so the next CUDA call does not report it
+      return nullptr;
+    }
     ptrs[dev] = static_cast<unsigned*>(p);
   }
   return ptrs[dev];
 }
 
-static int device_ok() {
+int device_ok() {
   static int ok_dev[64] = {};  // 0 unknown, 1 sm_100, 2 other
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
@@ -128,7 +134,7 @@ static size_t decode_workspace_bound(int64_t batch, int64_t h, int64_t hkv, int6
   return p.bytes;
 }
 
-static bool desc_ok(const eb_attn_desc* d) {
+bool desc_ok(const eb_attn_desc* d) {
   if (!d) return false;
   if (d->n_heads <= 0 || d->n_kv_heads <= 0 || d->n_heads % d->n_kv_heads) return false;
   if (d->head_dim <= 0 || d->head_dim > 256 || (d->head_dim & 1)) return false;
@@ -223,6 +229,7 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
       a.ws_acc = reinterpret_cast<float*>(w + p.acc_off);
     }
     a.err = error_word_ptr();
+    if (!a.err) return EB_ERR_CUDA;
     return cuda_status(launch_decode(a, d->dtype_cache, (int)batch, st));
   }
   // SIMT path: K/V prep writes the cache row, then attention over the cache.
@@ -769,6 +776,9 @@ int eb_get_device_error(uint32_t* bits) {
   if (cudaMemcpy(&v, p, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return EB_ERR_CUDA;
   const unsigned zero = 0;
   if (cudaMemcpy(p, &zero, sizeof(zero), cudaMemcpyHostToDevice) != cudaSuccess) return EB_ERR_CUDA;
+  // A kernel that gave up may have left split-K tickets behind in the
+  // library's own no-workspace scratch; put them back to zero for its next call.
+  if (v && !noalloc_clear_tickets()) return EB_ERR_CUDA;
   *bits = v;
   return v ? EB_ERR_DEVICE_TIMEOUT : EB_OK;
 }

@@ -116,27 +116,43 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with parity `parity` of barrier `bar` to complete, for at
-// most kWaitTimeoutNs. On timeout: set `err_bit` in the device error word, raise
-// the CTA's abort flag, return false. Returns false at once if the abort flag
-// is already raised, or if any CTA has already set the device error word, so
-// one stuck partner ends every role's loop (in every CTA) promptly.
+// most timeout_ns. On timeout: set `err_bit` in the device error word, raise
+// the CTA's abort flag, return false. Returns false early if the CTA's abort
+// flag is raised, or, once the wait has lasted kErrPollNs, if any CTA has set
+// the device error word, so one stuck partner ends every role's loop (in
+// every CTA) well before the limit.
+//
+// The poll loop touches only the barrier and, every 8th try, the abort flag
+// (shared memory). The clock is read every 64th try and the error word (a
+// global load that takes hundreds of cycles to return) only after kErrPollNs:
+// a load in flight when the phase completes would delay this thread by its
+// whole latency, and pipeline waits are short and frequent.
+constexpr unsigned long long kErrPollNs = 20000ull;
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          unsigned* err_word, unsigned err_bit) {
+                                          unsigned* err_word, unsigned err_bit,
+                                          unsigned long long timeout_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  for (;;) {
-#pragma unroll 1
-    for (int i = 0; i < 32; i++)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (*reinterpret_cast<volatile unsigned*>(err_word) != 0u) {
-      *abort_flag = 1;
-      return false;
-    }
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
-      atomicOr(err_word, err_bit);
-      *abort_flag = 1;
-      return false;
+  unsigned long long t0 = 0;
+  for (uint32_t spin = 1;; spin++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 7u) == 0u && *abort_flag) return false;
+    if ((spin & 63u) == 0u) {
+      const unsigned long long now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+        continue;
+      }
+      const unsigned long long el = now - t0;
+      if (el < kErrPollNs) continue;
+      if (*reinterpret_cast<volatile unsigned*>(err_word) != 0u) {
+        *abort_flag = 1;
+        return false;
+      }
+      if (el > timeout_ns) {
+        atomicOr(err_word, err_bit);
+        *abort_flag = 1;
+        return false;
+      }
     }
   }
 }

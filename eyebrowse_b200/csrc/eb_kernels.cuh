@@ -136,6 +136,15 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
 // Workspace bytes the split-K plan of one decode call at max_pos needs (0 when
 // it does not split), defined in eb_api.cu.
 size_t decode_plan_bytes(const eb_attn_desc* d, int64_t batch, int64_t max_pos);
+// Host-side checks shared by every entry point, defined in eb_api.cu: the
+// descriptor's shape, dtype codes, strides and window are valid; the current
+// device is an sm_100 part.
+bool desc_ok(const eb_attn_desc* d);
+int device_ok();
+// Zeroes the split-K tickets of eb_attention_decode_noalloc's scratch on the
+// current device (synchronously); false if a CUDA call failed. Defined in
+// eb_noalloc.cu.
+bool noalloc_clear_tickets();
 
 // ------------------------------------------------------------- prefill (tcgen05)
 struct PrefillArgs {

@@ -299,22 +299,23 @@ struct Attention {
     l.rope_sin = static_cast<const float*>(rope.sin.ptr());
     return l;
   }
-  // attention.rs:30-45: x [rows, hidden] at positions base_pos.. -> [rows, hidden].
-  // A fresh multi-row prompt (base_pos 0, rows > 1) takes the prefill path,
-  // anything else one decode step (one row), as in the reference.
+  // attention.rs:30-45: x [rows, hidden] at positions base_pos.. A fresh
+  // multi-row prompt (base_pos 0, rows > 1) takes the prefill path and
+  // returns [rows, hidden]; anything else is one decode step at base_pos,
+  // which, as the reference's decode (attention.rs:120-130) does, projects
+  // only the first row of x and returns [1, hidden].
   Tensor forward(Recorder& rec, const Tensor& x, const Rope& rope, KvCache& kv, size_t layer_idx,
                  size_t rows, size_t base_pos) const {
     if (!q_proj || !k_proj || !v_proj || !o_proj)
       throw Error("Attention::forward: projections not set", EB_ERR_INVALID_ARGUMENT);
     const bool is_prefill = base_pos == 0 && rows > 1;
-    if (!is_prefill && rows != 1)
-      throw Error("Attention::forward: a decode step takes one row", EB_ERR_INVALID_ARGUMENT);
-    const Tensor q = q_proj->forward(rec, x, rows);
-    const Tensor k = k_proj->forward(rec, x, rows);
-    const Tensor v = v_proj->forward(rec, x, rows);
+    const size_t n = is_prefill ? rows : 1;
+    const Tensor q = q_proj->forward(rec, x, n);
+    const Tensor k = k_proj->forward(rec, x, n);
+    const Tensor v = v_proj->forward(rec, x, n);
     const Tensor o = is_prefill ? prefill(rec, q, k, v, rope, kv, layer_idx, rows)
                                 : decode(rec, q, k, v, rope, kv, layer_idx, base_pos);
-    return o_proj->forward(rec, o, rows);
+    return o_proj->forward(rec, o, n);
   }
   // q [seq, n_heads*hd], k/v [seq, n_kv_heads*hd] -> o [seq, n_heads*hd]
   Tensor prefill(Recorder& rec, const Tensor& q, const Tensor& k, const Tensor& v,

@@ -269,8 +269,12 @@ EB_API int eb_workspace_init(void* workspace, size_t workspace_bytes, eb_stream_
  * looks up the array's device address (cudaGetSymbolAddress), so make that
  * first call before any stream capture. All calls on a device share the one
  * array: calls that overlap on the GPU (other streams, other threads) race
- * and corrupt each other's results; serialise them. Same arguments and
- * results as eb_attention_decode otherwise. */
+ * and corrupt each other's results; serialise them. The array keeps the last
+ * call's contents; its split-K tickets, which must start at zero, are zero
+ * when the library loads and every completed call leaves them at zero. A
+ * call whose kernel gave up (see eb_get_device_error) can leave them set:
+ * eb_get_device_error zeroes them when it reports such a failure. Same
+ * arguments, argument checks and results as eb_attention_decode otherwise. */
 EB_API int eb_attention_decode_noalloc(const eb_attn_desc* desc, const eb_attn_layer* layer,
                                        int64_t pos, const void* q, const void* k, const void* v,
                                        void* kcache, void* vcache, void* o, eb_stream_t stream);
@@ -295,7 +299,10 @@ EB_API int eb_head_broadcast(const void* local, void* multicast, int64_t rows,
 
 /* Returns and clears the device-side error word of the current device: a
  * non-zero value means some kernel's bounded wait gave up (the kernel then
- * returned early and its output is invalid). Synchronises the device. */
+ * returned early and its output is invalid). Synchronises the device. When
+ * it reports a failure it also zeroes the split-K tickets in the scratch of
+ * eb_attention_decode_noalloc. (A caller workspace shared by the failed call
+ * needs eb_workspace_init again.) */
 EB_API int eb_get_device_error(uint32_t* bits);
 
 #ifdef __cplusplus

@@ -10,6 +10,7 @@
 #include <math.h>
 #include <pthread.h>
 #include <stdatomic.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -183,6 +184,33 @@ void orc_linear(const float* x, const float* w, float* y, size_t m, size_t in_f,
     }
 }
 
+/* malloc that stops the process with a message instead of returning NULL
+ * (test infrastructure: an oracle that ran out of memory has no answer). */
+static void* xmalloc(size_t n) {
+  void* p = malloc(n ? n : 1);
+  if (!p) {
+    fprintf(stderr, "eb_oracle: out of memory (%zu bytes)\n", n);
+    abort();
+  }
+  return p;
+}
+
+/* Runs fn(arg) on the calling thread and on up to nthreads - 1 helper
+ * threads. The workers share an atomic job counter, so the job completes even
+ * when no helper can be started; only the helpers that started are joined. */
+static void run_workers(void* (*fn)(void*), void* arg, int nthreads) {
+  pthread_t* th = nthreads > 1 ? (pthread_t*)malloc(sizeof(pthread_t) * (size_t)(nthreads - 1)) : NULL;
+  int started = 0;
+  if (th)
+    for (int t = 0; t < nthreads - 1; t++) {
+      if (pthread_create(&th[started], NULL, fn, arg) != 0) break;
+      started++;
+    }
+  fn(arg);
+  for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
+  free(th);
+}
+
 typedef struct {
   const float *x, *w;
   float* y;
@@ -211,11 +239,7 @@ void orc_linear_threaded(const float* x, const float* w, float* y, size_t m, siz
   jb.x = x; jb.w = w; jb.y = y; jb.m = m; jb.in_f = in_f; jb.out_f = out_f;
   atomic_init(&jb.next, 0);
   if (nthreads < 1) nthreads = 1;
-  if (nthreads == 1) { linear_worker(&jb); return; }
-  pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)nthreads);
-  for (int t = 0; t < nthreads; t++) pthread_create(&th[t], NULL, linear_worker, &jb);
-  for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
-  free(th);
+  run_workers(linear_worker, &jb, nthreads);
 }
 
 /* One (query row, head) of the two-pass attention in testutil.rs:142-169.
@@ -256,7 +280,7 @@ void orc_attn_prefill_window(const float* q, const float* k, const float* v, flo
                              size_t window) {
   /* crates/eyebrowse-kernels/src/testutil.rs:130-172, keys from window_lo(i) */
   size_t group = h / hkv;
-  float* scores = (float*)malloc(sizeof(float) * (s ? s : 1));
+  float* scores = (float*)xmalloc(sizeof(float) * (s ? s : 1));
   for (size_t i = 0; i < s; i++) {
     size_t lo = window_lo(i, window);
     for (size_t hh = 0; hh < h; hh++) {
@@ -285,7 +309,7 @@ typedef struct {
 static void* prefill_worker(void* arg) {
   prefill_job* jb = (prefill_job*)arg;
   size_t group = jb->h / jb->hkv;
-  float* scores = (float*)malloc(sizeof(float) * (jb->s ? jb->s : 1));
+  float* scores = (float*)xmalloc(sizeof(float) * (jb->s ? jb->s : 1));
   for (;;) {
     /* rows handed out longest-first so the causal triangle balances */
     size_t t = atomic_fetch_add(&jb->next, 1);
@@ -316,11 +340,7 @@ void orc_attn_prefill_part(const float* q, const float* k, const float* v, float
   jb.scale = scale;
   atomic_init(&jb.next, 0);
   if (nthreads < 1) nthreads = 1;
-  if (nthreads == 1) { prefill_worker(&jb); return; }
-  pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)nthreads);
-  for (int t = 0; t < nthreads; t++) pthread_create(&th[t], NULL, prefill_worker, &jb);
-  for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
-  free(th);
+  run_workers(prefill_worker, &jb, nthreads);
 }
 
 void orc_attn_decode_window(const float* q, const float* kc, const float* vc, float* o,
@@ -330,7 +350,7 @@ void orc_attn_decode_window(const float* q, const float* kc, const float* vc, fl
   (void)max_seq;
   size_t group = h / hkv;
   size_t lo = window_lo(pos, window);
-  float* scores = (float*)malloc(sizeof(float) * (pos + 1));
+  float* scores = (float*)xmalloc(sizeof(float) * (pos + 1));
   for (size_t hh = 0; hh < h; hh++) {
     size_t kvh = hh / group;
     size_t qbase = hh * hd;
@@ -358,7 +378,7 @@ typedef struct {
 static void* decode_worker(void* arg) {
   decode_job* jb = (decode_job*)arg;
   size_t group = jb->h / jb->hkv;
-  float* scores = (float*)malloc(sizeof(float) * jb->max_seq);
+  float* scores = (float*)xmalloc(sizeof(float) * jb->max_seq);
   for (;;) {
     size_t t = atomic_fetch_add(&jb->next, 1);
     if (t >= jb->batch * jb->h) break;
@@ -385,15 +405,11 @@ void orc_attn_decode_batched(const float* q, const float* kc, const float* vc, f
   jb.cache_stride = cache_stride; jb.scale = scale;
   atomic_init(&jb.next, 0);
   if (nthreads < 1) nthreads = 1;
-  if (nthreads == 1) { decode_worker(&jb); return; }
-  pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * (size_t)nthreads);
-  for (int t = 0; t < nthreads; t++) pthread_create(&th[t], NULL, decode_worker, &jb);
-  for (int t = 0; t < nthreads; t++) pthread_join(th[t], NULL);
-  free(th);
+  run_workers(decode_worker, &jb, nthreads);
 }
 
 static float* dup(const float* x, size_t n) {
-  float* y = (float*)malloc(sizeof(float) * (n ? n : 1));
+  float* y = (float*)xmalloc(sizeof(float) * (n ? n : 1));
   memcpy(y, x, sizeof(float) * n);
   return y;
 }

@@ -63,6 +63,20 @@ def test_host_validation_precedes_device_work(eb):
     neg = eb.make_desc(16, 8, 128, 4096, window=-1)  # a window is a row count
     assert L.eb_attention_prefill(ctypes.byref(neg), ctypes.byref(lay), 4, 1, 1, 1, 1, 1, 1, None,
                                   0, None) == 1
+    # the no-workspace decode checks the descriptor as eb_attention_decode
+    # does: an unknown dtype code (here 7) is refused before any device work
+    for field in ("dtype_qkv", "dtype_cache", "dtype_out"):
+        bad_dt = eb.make_desc(16, 8, 128, 4096)
+        setattr(bad_dt, field, 7)
+        assert L.eb_attention_decode_noalloc(ctypes.byref(bad_dt), ctypes.byref(lay), 5, 16, 16,
+                                             16, 16, 16, 16, None) == 1, field
+        assert L.eb_attention_decode(ctypes.byref(bad_dt), ctypes.byref(lay), 5, 16, 16, 16, 16,
+                                     16, 16, None, 0, None) == 1, field
+    neg_stride = eb.make_desc(16, 8, 128, 4096, q_stride=-4)
+    assert L.eb_attention_decode_noalloc(ctypes.byref(neg_stride), ctypes.byref(lay), 5, 16, 16,
+                                         16, 16, 16, 16, None) == 1
+    assert L.eb_attention_decode_noalloc(ctypes.byref(d), ctypes.byref(lay), 4096, 16, 16, 16, 16,
+                                         16, 16, None) == 1  # pos >= max_seq
     # linear_f16w: shapes are checked before anything else; m = 0 is a no-op
     assert L.eb_linear_f16w(16, 16, 16, -1, 64, 64, None, 0, None) == 1
     assert L.eb_linear_f16w(16, 16, 16, 4, 0, 64, None, 0, None) == 1
