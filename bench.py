@@ -321,7 +321,14 @@ class PrefillWork:
         else:
             self.full = self.o
             self.launches_per_step = 3  # K/V prep, q prep, attention
+        if self.q_in_kernel():
+            self.launches_per_step -= 1  # q normalised and rotated inside the attention kernel
         self.bytes_in = sum(t.numel() * t.element_size() for t in (self.q, self.k, self.v))
+
+    def q_in_kernel(self):
+        """q already in the cache's 16-bit type: the attention kernel transforms
+        its query tiles itself (no q row-prep launch)."""
+        return self.dt != 0
 
     def step(self):
         eb = self.eb

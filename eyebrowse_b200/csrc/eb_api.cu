@@ -505,10 +505,18 @@ int eb_rope_tables(float* cos_t, float* sin_t, int64_t max_seq, int64_t head_dim
 }
 
 // ---------------------------------------------------------------- fused primitive
+// q rows already in the 16-bit operand type are normalised and rotated
+// inside the attention kernel (no staging); others go through the row-prep
+// pass into the workspace.
+static bool q_fused_path(const eb_attn_desc* d) {
+  return d->dtype_cache != EB_F32 && d->dtype_qkv == d->dtype_cache;
+}
+
 size_t eb_attention_prefill_workspace_bytes(const eb_attn_desc* d, int64_t seq) {
   if (!desc_ok(d) || seq <= 0) return 0;
   if (!prefill_tc_supported(d->head_dim)) return 0;
   const bool split = d->dtype_cache == EB_F32;
+  if (q_fused_path(d)) return 0;
   return (split ? kv_split_bytes(seq, d->n_kv_heads, d->head_dim) : 0) +
          q_prep_bytes(seq, d->n_heads, d->head_dim, split);
 }
@@ -523,7 +531,7 @@ static int prefill_check(const eb_attn_desc* d, const eb_attn_layer* L, int64_t 
   if (seq == 0) return EB_OK;
   if (prefill_tc_supported(d->head_dim)) {
     const size_t need = eb_attention_prefill_workspace_bytes(d, seq);
-    if (!ws || ws_bytes < need || !aligned16(ws)) return EB_ERR_WORKSPACE;
+    if (need > 0 && (!ws || ws_bytes < need || !aligned16(ws))) return EB_ERR_WORKSPACE;
   }
   return EB_OK;
 }
@@ -587,31 +595,43 @@ static int prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, int64_t
     if (!aligned16(q) || !aligned16(o) || !aligned16(kcache) || !aligned16(vcache) ||
         ((qs_of(d) * eq) & 15) || ((os_of(d) * eo) & 15))
       return EB_ERR_INVALID_ARGUMENT;
+    const bool fused = q_fused_path(d);
     // q -> RMSNorm(q_norm_w) -> RoPE -> the MMA operand type (or f16 hi/lo
-    // planes), the same row transform the k rows get
-    void* qprep = static_cast<char*>(workspace) +
-                  (split ? kv_split_bytes(seq, d->n_kv_heads, hd) : 0);
-    PrepArgs qa{};
-    qa.k = q;
-    qa.dtype_kv = d->dtype_qkv;
-    qa.kv_stride = qs_of(d);
-    qa.kcache = split ? nullptr : qprep;
-    qa.dtype_cache = d->dtype_cache;
-    qa.split = split ? qprep : nullptr;
-    qa.rows = (int)seq;
-    qa.hkv = d->n_heads;
-    qa.hd = hd;
-    qa.k_norm_w = L ? L->q_norm_w : nullptr;
-    qa.cos_t = cos_t;
-    qa.sin_t = sin_t;
-    qa.eps = d->eps;
-    qa.batch = 1;
-    cudaError_t e = launch_prep_kv(qa, st);
-    if (e != cudaSuccess) return cuda_status(e);
+    // planes), the same row transform the k rows get: inside the attention
+    // kernel when q already has the operand type, else a row pass into the
+    // workspace
+    void* qprep = fused ? const_cast<void*>(q)
+                        : static_cast<char*>(workspace) +
+                              (split ? kv_split_bytes(seq, d->n_kv_heads, hd) : 0);
+    if (!fused) {
+      PrepArgs qa{};
+      qa.k = q;
+      qa.dtype_kv = d->dtype_qkv;
+      qa.kv_stride = qs_of(d);
+      qa.kcache = split ? nullptr : qprep;
+      qa.dtype_cache = d->dtype_cache;
+      qa.split = split ? qprep : nullptr;
+      qa.rows = (int)seq;
+      qa.hkv = d->n_heads;
+      qa.hd = hd;
+      qa.k_norm_w = L ? L->q_norm_w : nullptr;
+      qa.cos_t = cos_t;
+      qa.sin_t = sin_t;
+      qa.eps = d->eps;
+      qa.batch = 1;
+      cudaError_t e = launch_prep_kv(qa, st);
+      if (e != cudaSuccess) return cuda_status(e);
+    }
     PrefillArgs a{};
     a.o = o;
     a.dtype_o = d->dtype_out;
     a.o_stride = os_of(d);
+    a.q_fused = fused ? 1 : 0;
+    a.q_stride = qs_of(d);
+    a.q_norm_w = L ? L->q_norm_w : nullptr;
+    a.cos_t = cos_t;
+    a.sin_t = sin_t;
+    a.eps = d->eps;
     GatherSpec gs{};
     if (g) {
       a.o = nullptr;

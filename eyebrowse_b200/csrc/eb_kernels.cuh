@@ -160,6 +160,18 @@ struct PrefillArgs {
   // TMA through the destination tensor maps passed beside the arguments.
   int n_dst;
   int h_off;
+  // Query rows transformed inside the kernel (q_fused != 0): q16 is the raw
+  // q [S][H][hd] in the operand type with rows q_stride elements apart; each
+  // tile's rows are normalised (q_norm_w, if non-null) and rotated (cos_t /
+  // sin_t [*, hd/2], if non-null) in shared memory after their TMA load,
+  // with the row-prep pass's f32 arithmetic. Otherwise q16 holds rows the
+  // row-prep pass already transformed.
+  int q_fused;
+  int64_t q_stride;
+  const float* q_norm_w;
+  const float* cos_t;
+  const float* sin_t;
+  float eps;
 };
 // Destinations of a head gather: up to kMaxGather buffers [S][H_total][hd]
 // in the output dtype (this GPU's and its peers', mapped here).

@@ -94,6 +94,107 @@ struct GatherMaps {
 
 
 
+// Fused q prep: thread r of a query tile's softmax warpgroup turns its row
+// of the TMA-loaded raw query tile (HD 16-bit values in 128-byte-swizzled
+// boxes of 64) into the MMA operand: RMSNorm (q_norm_w), then half-split
+// RoPE at position q_row, then rounding to the operand type -- the row-prep
+// pass's per-element f32 arithmetic (crates/eyebrowse-kernels/src/
+// rmsnorm.rs:34-36, rope.rs:25-30) on the same values, with the sum of
+// squares in one thread's order. The table row is fetched (up to 32 pairs at
+// a time) before the tile lands. Rows past S (zero-filled by TMA) are left
+// as they are. Then the
+// generic-proxy writes are made visible to the tensor core and the tile's
+// ready barrier (128 arrivals) is arrived on.
+template <int HD, bool BF16>
+__device__ __forceinline__ void q_tile_transform(uint32_t tile, int r, int q_row,
+                                                 const PrefillArgs& a, uint32_t q_bar,
+                                                 uint32_t ready_bar, volatile int* abort_flag) {
+  constexpr int HALF = HD / 2, NCH = HD / 8;  // 8-element chunks per row
+  const bool valid = q_row < a.S;
+  const bool rope = valid && a.cos_t != nullptr;
+  const bool norm = valid && a.q_norm_w != nullptr;
+  const float* crow = rope ? a.cos_t + (int64_t)q_row * HALF : nullptr;
+  const float* srow = rope ? a.sin_t + (int64_t)q_row * HALF : nullptr;
+  auto chunk_addr = [&](int c) {  // chunk c (elements 8c..8c+7) of row r
+    return tile + (uint32_t)(c >> 3) * (128u * 128u) + sw128_offset((uint32_t)r, (uint32_t)(c & 7));
+  };
+  auto load8 = [&](int c, float (&f)[8]) {
+    uint32_t w[4];
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3])
+                 : "r"(chunk_addr(c)));
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float2 v = BF16 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]))
+                            : __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+      f[2 * k] = v.x;
+      f[2 * k + 1] = v.y;
+    }
+  };
+  // The row's table entries come in passes of up to 32 pairs, all loads of a
+  // pass in flight at once; the first pass's while the tile lands.
+  constexpr int PP = HALF < 32 ? HALF : 32;  // pairs per pass
+  constexpr int NPASS = HALF / PP;
+  float cs[PP], sn[PP];
+  auto fetch = [&](int pass) {
+#pragma unroll
+    for (int i = 0; i < PP; i += 4) {
+      const float4 c4 = rope ? *reinterpret_cast<const float4*>(crow + pass * PP + i)
+                             : make_float4(1.f, 1.f, 1.f, 1.f);
+      const float4 s4 = rope ? *reinterpret_cast<const float4*>(srow + pass * PP + i)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      cs[i] = c4.x; cs[i + 1] = c4.y; cs[i + 2] = c4.z; cs[i + 3] = c4.w;
+      sn[i] = s4.x; sn[i + 1] = s4.y; sn[i + 2] = s4.z; sn[i + 3] = s4.w;
+    }
+  };
+  if (rope) fetch(0);
+  const bool got_q = mbar_wait(q_bar, 0, abort_flag, a.err, kErrTimeoutSoftmax);
+  if (got_q && (rope || norm)) {
+    float inv = 1.f;
+    if (norm) {
+      float ss = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < NCH; c++) {
+        float f[8];
+        load8(c, f);
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss = __fadd_rn(ss, __fmul_rn(f[e], f[e]));
+      }
+      inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+    }
+#pragma unroll 1
+    for (int pass = 0; pass < NPASS; pass++) {
+      if (rope && pass > 0) fetch(pass);
+#pragma unroll
+      for (int cc = 0; cc < PP / 8; cc++) {  // chunk c (first half) with its partner c + NCH/2
+        const int c = pass * (PP / 8) + cc;
+        float x1[8], x2[8];
+        load8(c, x1);
+        load8(c + NCH / 2, x2);
+        if (norm) {
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            x1[e] = __fmul_rn(__fmul_rn(x1[e], inv), a.q_norm_w[8 * c + e]);
+            x2[e] = __fmul_rn(__fmul_rn(x2[e], inv), a.q_norm_w[HALF + 8 * c + e]);
+          }
+        }
+        if (rope) {
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            const float u = x1[e], v = x2[e], co = cs[8 * cc + e], si = sn[8 * cc + e];
+            x1[e] = __fsub_rn(__fmul_rn(u, co), __fmul_rn(v, si));
+            x2[e] = __fadd_rn(__fmul_rn(v, co), __fmul_rn(u, si));
+          }
+        }
+        st_chunk<BF16>(chunk_addr(c), x1);
+        st_chunk<BF16>(chunk_addr(c + NCH / 2), x2);
+      }
+    }
+    fence_async_smem();
+  }
+  mbar_arrive(ready_bar);
+}
+
 // WIN: a sliding window narrower than the sequence (a.window). Its own
 // instantiation, so the plain causal kernel carries none of the window's
 // index arithmetic.
@@ -126,7 +227,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
   constexpr int kKEmpty0 = kKFull0 + NSTK;        // [NSTK]
   constexpr int kVFull0 = kKEmpty0 + NSTK;        // [NSTV]
   constexpr int kVEmpty0 = kVFull0 + NSTV;        // [NSTV]
-  constexpr int kNumBars = kVEmpty0 + NSTV;
+  constexpr int kQReady0 = kVEmpty0 + NSTV;       // [NQ]: tile t's rows transformed in smem
+  constexpr int kNumBars = kQReady0 + NQ;
   static_assert(kNumBars * 8 <= 384, "barrier area");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -147,7 +249,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     mbar_init(bar(kBarFinal), 1);
     for (int i = kSFull0; i < kPFull0; i++) mbar_init(bar(i), 1);
     for (int i = kPFull0; i < kODone0; i++) mbar_init(bar(i), 128);  // P and P-half-0
-    for (int i = kODone0; i < kNumBars; i++) mbar_init(bar(i), 1);
+    for (int i = kODone0; i < kQReady0; i++) mbar_init(bar(i), 1);
+    for (int i = kQReady0; i < kNumBars; i++) mbar_init(bar(i), 128);  // the tile's rows
     *abort_flag = 0;
     fence_mbar_init();
     fence_async_smem();
@@ -278,16 +381,21 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
           }
         }
       };
-      bool ok = mbar_wait(bar(kBarQ), 0, abort_flag, a.err, kErrTimeoutMma);
-      tc_fence_after();
+      // The query tiles: landed (TMA), or landed and then transformed in
+      // shared memory by their softmax warpgroups (fused q prep).
+      bool ok = a.q_fused ? true : mbar_wait(bar(kBarQ), 0, abort_flag, a.err, kErrTimeoutMma);
       if (ok && mbar_wait(bar(kKFull0), 0, abort_flag, a.err, kErrTimeoutMma)) {
-        tc_fence_after();
 #pragma unroll
         for (int t = 0; t < NQ; t++) {
+          if (a.q_fused && !mbar_wait(bar(kQReady0 + t), 0, abort_flag, a.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           issue_qk(t, 0, 0);
           umma_commit(bar(kSFull0 + t * NSB));
         }
-        umma_commit(bar(kKEmpty0));
+        if (ok) umma_commit(bar(kKEmpty0));
       } else {
         ok = false;
       }
@@ -339,7 +447,9 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
           } else {
             issue_pv(t, j % NSB, sv, j == 0, 0, BN / 16);
           }
-          umma_commit(bar(kODone0 + t));
+          // With one S buffer the softmax learns that PV_t(j) is done from
+          // S_t(j+1), committed after it (below); two buffers need a barrier.
+          if constexpr (NSB == 2) umma_commit(bar(kODone0 + t));
           if (NSB == 1 && nj < n_tiles) {
             // S_t(j+1) overwrites P_t(j): issued after PV_t(j), executed in order
             if (t == 0 &&
@@ -371,6 +481,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const float sl2 = a.scale_log2;
     const uint32_t tO = tmem + lane_off + t * HD;
+    if (a.q_fused) q_tile_transform<HD, BF16>(sQ + t * C::QT_BYTES, r, q_row, a, bar(kBarQ),
+                                             bar(kQReady0 + t), abort_flag);
     // With a window the running max starts finite: a row can see no key of
     // its first tiles (S row all -inf), and -inf - (-inf) would turn its P
     // into NaN. Any finite score later rescales by ex2(-1e30 - m) = 0.
@@ -432,11 +544,13 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         const float m_new = fmaxf(m_run, ms);
         const float corr = ex2(m_run - m_new);
         if (j > 0) {
-          // PV(j-1) done. Sound as a parity wait: s_full(j) implies PV(0..j-2)
-          // completed (QK(j) is issued after PV(j-2)) and PV(j) needs P(j),
-          // so at most one phase is outstanding here.
-          const bool got_o = mbar_wait(bar(kODone0 + t), (j - 1) & 1, abort_flag, a.err,
-                                       kErrTimeoutSoftmax);
+          // PV(j-1) done. With one S buffer, S(j) (waited above) was committed
+          // after PV(j-1), so it is. With two, a parity wait on the PV barrier
+          // is sound: s_full(j) implies PV(0..j-2) completed (QK(j) is issued
+          // after PV(j-2)) and PV(j) needs P(j), so at most one phase is
+          // outstanding here.
+          const bool got_o = NSB == 1 || mbar_wait(bar(kODone0 + t), (j - 1) & 1, abort_flag,
+                                                   a.err, kErrTimeoutSoftmax);
           __syncwarp();
           if (!__all_sync(0xffffffffu, got_o)) {
             ok = false;
@@ -677,6 +791,24 @@ bool make_kv_map(CUtensorMap* m, const void* base, int S, int Hkv, int hd, int B
   return r == CUDA_SUCCESS;
 }
 
+// 3-D map over raw query rows [S][H][hd] (16-bit) whose rows are row_stride
+// elements apart (a fused q/k/v projection output is read in place), box
+// {64, 1, 128}, 128-byte swizzle.
+static bool make_q_map(CUtensorMap* m, const void* base, int S, int H, int hd,
+                       int64_t row_stride, bool bf16) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)H, (cuuint64_t)S};
+  cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)row_stride * 2};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // 3-D map over a gathered output [S][H_total][hd] of dtype dt (16-bit or
 // f32), box {128 bytes of one head row, 1 head, 128 rows}, 128-byte swizzle.
 static bool make_out_map(CUtensorMap* m, uint64_t base, int S, int64_t h_total, int hd, int dt) {
@@ -717,6 +849,9 @@ static cudaError_t run_prefill_k(const PrefillArgs& a, const void* q16, const vo
     if (!make_kv_map(&mq, qp, a.S, a.H, HD, 128, false) ||
         !make_kv_map(&mql, qp + (size_t)a.S * a.H * HD, a.S, a.H, HD, 128, false))
       return cudaErrorInvalidValue;
+  } else if (a.q_fused) {
+    if (!make_q_map(&mq, q16, a.S, a.H, HD, a.q_stride, BF16)) return cudaErrorInvalidValue;
+    mql = mq;
   } else {
     if (!make_kv_map(&mq, q16, a.S, a.H, HD, 128, BF16)) return cudaErrorInvalidValue;
     mql = mq;

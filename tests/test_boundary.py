@@ -131,7 +131,11 @@ def test_workspace_sizes(eb):
     assert eb.attn_prefill_workspace_bytes(16, 8, 128, 128) == (4 * 128 * 8 + 2 * 128 * 16) * 128 * 2
     assert eb.attn_prefill_workspace_bytes(2, 1, 5, 8) == 0  # SIMT path
     f16 = eb.make_desc(32, 8, 128, 8192, dtype_qkv=eb.EB_F16, dtype_cache=eb.EB_F16)
-    # reads the f16 cache directly; stages only the prepared f16 q rows
-    assert eb.attention_prefill_workspace_bytes(f16, 8192) == 8192 * 32 * 128 * 2
+    # f16 q and cache: q is normalised and rotated inside the attention
+    # kernel, the cache is read directly: nothing is staged
+    assert eb.attention_prefill_workspace_bytes(f16, 8192) == 0
+    mixed = eb.make_desc(32, 8, 128, 8192, dtype_qkv=eb.EB_F32, dtype_cache=eb.EB_F16)
+    # f32 q for an f16 cache: the row pass stages the f16 q rows
+    assert eb.attention_prefill_workspace_bytes(mixed, 8192) == 8192 * 32 * 128 * 2
     odd = eb.make_desc(4, 2, 96, 64, dtype_qkv=eb.EB_F16, dtype_cache=eb.EB_F16)
     assert eb.attention_prefill_workspace_bytes(odd, 64) == 0  # SIMT path
