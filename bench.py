@@ -53,19 +53,51 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
+# The CUDA sources each profiled kernel is built from. A profile's traffic
+# line records their hash; once a source changes, the recorded figure no
+# longer describes the shipping kernel and the bench reports null instead.
+KERNEL_SOURCES = {
+    "prefill_cfg3": ("eb_prefill.cu", "eb_common.cuh", "eb_tc.cuh"),
+    "prefill_cfg4": ("eb_prefill.cu", "eb_common.cuh", "eb_tc.cuh"),
+    "prep_cfg3": ("eb_small.cu", "eb_rowops.cuh", "eb_common.cuh"),
+    "decode_cfg5": ("eb_decode_tc.cu", "eb_common.cuh", "eb_tc.cuh"),
+    "decode_cfg2": ("eb_decode.cu", "eb_common.cuh", "eb_rowops.cuh"),
+    "linear_proj3": ("eb_linear.cu", "eb_common.cuh", "eb_tc.cuh"),
+}
+
+
+def source_hash(key: str):
+    """sha256 (first 16 hex digits) of the kernel sources behind `key`."""
+    import hashlib
+    names = KERNEL_SOURCES.get(key)
+    if not names:
+        return None
+    h = hashlib.sha256()
+    for n in names:
+        with open(os.path.join(ROOT, "eyebrowse_b200", "csrc", n), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:16]
+
+
 def profile_traffic(key: str):
     """Per-launch DRAM traffic recorded from an ncu capture in profiles/*.md
-    (a line `traffic[<key>]: <bytes per launch>`), or None."""
+    (a line `traffic[<key>]: <bytes per launch> ... source <hash>`), or None
+    when there is none or it was captured from other kernel sources."""
     d = os.path.join(ROOT, "profiles")
     if not os.path.isdir(d):
         return None
+    want = source_hash(key)
     for fn in sorted(os.listdir(d)):
         if not fn.endswith(".md"):
             continue
         for line in open(os.path.join(d, fn)):
             if line.startswith(f"traffic[{key}]:"):
+                words = line.split(":", 1)[1].split()
+                if want is None or "source" not in words or \
+                        words[words.index("source") + 1].strip("().,") != want:
+                    return None
                 try:
-                    return float(line.split(":", 1)[1].split()[0])
+                    return float(words[0])
                 except ValueError:
                     return None
     return None
@@ -607,30 +639,48 @@ class LinearWork:
                         "(upload, compute, download on separate streams)"}
 
 
-def cpu_baseline_linear(w: LinearWork, threads: int | None = None, target_s: float = 8.0):
-    """Oracle cpu_linear (the reference's loop order) on all host threads,
-    parallel over output features, over a bounded sample of output columns,
-    scaled to the workload's unit."""
+def _median_time(fn, reps: int) -> float:
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts)
+
+
+def _host_threads() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+def cpu_baseline_linear(w: LinearWork, threads: int | None = None, reps: int = 3):
+    """Oracle cpu_linear (the reference's loop order) on a fixed sample -- 8
+    rows (m, if smaller) x 2048 output features (all, if fewer) at the
+    workload's k -- on all host threads (parallel over output features) and
+    on one thread (256 features), median of `reps` timings each, scaled to
+    the workload's unit."""
     from oracle import oracle as orc
-    threads = threads or len(os.sched_getaffinity(0))
+    threads = threads or _host_threads()
     rng = np.random.default_rng(0)
     m = min(w.m, 8)
     x = rng.standard_normal((m, w.k)).astype(np.float32)
-    n = min(w.n, 256)
-    while True:
+
+    def measure(n, nt):
         wt = (rng.standard_normal((n, w.k)) * 0.02).astype(np.float16).astype(np.float32)
-        t0 = time.perf_counter()
-        orc.linear_threaded(x, wt, m, w.k, n, threads)
-        dt = time.perf_counter() - t0
-        if dt >= target_s / 4 or n >= w.n:
-            break
-        n = min(w.n, int(n * max(2.0, target_s / 2 / max(dt, 1e-4))))
-    flop, nbytes = 2.0 * m * n * w.k, 2.0 * n * w.k
-    value = flop / dt / 1e12 if w.bound == "tensor" else nbytes / dt / 1e9
-    return {"value": value, "unit": "TFLOP/s" if w.bound == "tensor" else "GB/s",
-            "cores": threads, "kind": "port",
-            "sample": f"oracle cpu_linear, {m} rows x {n} of {w.n} outputs, k={w.k} "
-                      f"({dt:.2f} s, f32, gcc -O3 -ffp-contract=off, {threads} threads)"}
+        dt = _median_time(lambda: orc.linear_threaded(x, wt, m, w.k, n, nt), reps)
+        flop, nbytes = 2.0 * m * n * w.k, 2.0 * n * w.k
+        return (flop / dt / 1e12 if w.bound == "tensor" else nbytes / dt / 1e9), dt
+
+    n_all, n_one = min(w.n, 2048), min(w.n, 256)
+    v_all, dt_all = measure(n_all, threads)
+    v_one, dt_one = measure(n_one, 1)
+    unit = "TFLOP/s" if w.bound == "tensor" else "GB/s"
+    return {"value": v_all, "unit": unit, "cores": threads, "kind": "port",
+            "sample": f"oracle cpu_linear, {m} rows x {n_all} of {w.n} outputs, k={w.k}; median of "
+                      f"{reps} ({dt_all:.2f} s each; f32, gcc -O3 -ffp-contract=off, {threads} "
+                      f"threads)",
+            "single_thread": {"value": v_one, "unit": unit, "cores": 1,
+                              "sample": f"{m} rows x {n_one} outputs; median of {reps} "
+                                        f"({dt_one:.2f} s each)"}}
 
 
 def make_workload(name, batch=None):
@@ -763,42 +813,49 @@ def _cpu_inputs(w: PrefillWork):
     return _CPU_INPUTS[key]
 
 
-def cpu_baseline_prefill(w: PrefillWork, target_s: float = 12.0, threads: int | None = None,
-                         sample=None):
-    """Oracle (the reference's CPU attention, restated) on the host cores over a
-    bounded sample: the last R query rows of the first Hs heads, grown until
-    the sample takes about target_s seconds. Pass `sample=(R, Hs)` to time a
-    fixed sample."""
+# Fixed CPU samples, the same in the bench arm and the reference arm: the last
+# `rows` query rows (the longest causal rows) of the first `heads` heads.
+PREFILL_SAMPLE_ALL = (1024, 8)   # all host threads, parallel over query rows
+PREFILL_SAMPLE_ONE = (128, 1)    # one thread: the single-threaded Rust loop's order
+
+
+def _prefill_sample(w: PrefillWork, sample, threads: int, reps: int):
     from oracle import oracle as orc
-    threads = threads or len(os.sched_getaffinity(0))
     S, H, Hkv, hd = w.S, w.H, w.Hkv, w.hd
     q, k, v = _cpu_inputs(w)
-    rows_n, nh = sample if sample else (min(S, 64), 1)
-    while True:
-        r0 = S - rows_n
-        t0 = time.perf_counter()
-        W = w.window if w.window and w.window < S else S
-        orc.attn_prefill_part(q, k, v, H, Hkv, S, hd, w.scale, (r0, S), (0, nh), threads,
-                              window=W if W < S else 0)
-        dt = time.perf_counter() - t0
-        flop = sum(4.0 * hd * min(i + 1, W) for i in range(r0, S)) * nh
-        if sample or dt >= target_s / 2 or (rows_n >= S and nh >= H):
-            break
-        grow = max(2.0, (target_s / 1.5) / max(dt, 1e-3))
-        if rows_n < S:
-            rows_n = min(S, int(rows_n * grow))
-        else:
-            nh = min(H, int(nh * grow) + 1)
-    return {"value": flop / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"oracle attn_prefill rows [{S - rows_n},{S}) x heads [0,{nh}) of "
-                      f"{w.name.split()[0]} ({flop:.3e} FLOP in {dt:.2f} s, f32, "
-                      f"gcc -O3 -ffp-contract=off, {threads} threads)",
-            "_sample": (rows_n, nh)}
+    rows_n, nh = min(S, sample[0]), min(H, sample[1])
+    r0 = S - rows_n
+    W = w.window if w.window and w.window < S else S
+    dt = _median_time(lambda: orc.attn_prefill_part(q, k, v, H, Hkv, S, hd, w.scale, (r0, S),
+                                                    (0, nh), threads,
+                                                    window=W if W < S else 0), reps)
+    flop = sum(4.0 * hd * min(i + 1, W) for i in range(r0, S)) * nh
+    return flop / dt / 1e12, dt, flop, rows_n, nh
 
 
-def cpu_baseline_decode(w: BatchedDecodeWork, threads: int | None = None, n_seq: int = 4):
+def cpu_baseline_prefill(w: PrefillWork, threads: int | None = None, reps: int = 3):
+    """Oracle attention (the reference's CPU attention, restated) on fixed
+    samples of the workload: PREFILL_SAMPLE_ALL on all host threads and
+    PREFILL_SAMPLE_ONE on one thread, median of `reps` timings each."""
+    threads = threads or _host_threads()
+    v_all, dt_all, f_all, r_all, h_all = _prefill_sample(w, PREFILL_SAMPLE_ALL, threads, reps)
+    v_one, dt_one, f_one, r_one, h_one = _prefill_sample(w, PREFILL_SAMPLE_ONE, 1, reps)
+    name = w.name.split()[0]
+    return {"value": v_all, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"oracle attn_prefill rows [{w.S - r_all},{w.S}) x heads [0,{h_all}) of "
+                      f"{name} ({f_all:.3e} FLOP, median of {reps}: {dt_all:.2f} s; f32, gcc -O3 "
+                      f"-ffp-contract=off, {threads} threads)",
+            "single_thread": {"value": v_one, "unit": "TFLOP/s", "cores": 1,
+                              "sample": f"rows [{w.S - r_one},{w.S}) x heads [0,{h_one}) "
+                                        f"({f_one:.3e} FLOP, median of {reps}: {dt_one:.2f} s)"}}
+
+
+DECODE_SAMPLE_ALL = 8   # sequences (the first of the workload's), all host threads
+DECODE_SAMPLE_ONE = 1   # one sequence, one thread
+
+
+def _decode_sample(w: BatchedDecodeWork, n_seq: int, threads: int, reps: int):
     from oracle import oracle as orc
-    threads = threads or len(os.sched_getaffinity(0))
     B = min(n_seq, w.B)
     ms = int(w.ctx[:B].max())
     rng = np.random.default_rng(1)
@@ -806,50 +863,65 @@ def cpu_baseline_decode(w: BatchedDecodeWork, threads: int | None = None, n_seq:
     vc = rng.standard_normal((B, ms, w.Hkv, w.hd)).astype(np.float32)
     q = rng.standard_normal((B, w.H, w.hd)).astype(np.float32)
     pos = w.pos[:B]
-    t0 = time.perf_counter()
-    orc.attn_decode_batched(q, kc, vc, pos, w.H, w.Hkv, w.hd, ms, ms * w.Hkv * w.hd,
-                            w.hd ** -0.5, nthreads=threads)
-    dt = time.perf_counter() - t0
-    es = 2  # bytes per element of the f16 cache the GPU streams
-    nbytes = 2.0 * (pos.astype(np.int64) + 1).sum() * w.Hkv * w.hd * es
-    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"oracle attn_decode on {B} of {w.B} sequences (f32 math, bytes counted "
-                      f"at f16 cache width), {dt:.2f} s, {threads} threads"}
+    dt = _median_time(lambda: orc.attn_decode_batched(q, kc, vc, pos, w.H, w.Hkv, w.hd, ms,
+                                                      ms * w.Hkv * w.hd, w.hd ** -0.5,
+                                                      nthreads=threads), reps)
+    nbytes = 2.0 * (pos.astype(np.int64) + 1).sum() * w.Hkv * w.hd * 2  # at the f16 cache width
+    return nbytes / dt / 1e9, dt, B
+
+
+def cpu_baseline_decode(w: BatchedDecodeWork, threads: int | None = None, reps: int = 3):
+    """Oracle decode on the workload's first DECODE_SAMPLE_ALL sequences (all
+    host threads, parallel over (sequence, head)) and on its first sequence
+    (one thread), median of `reps` timings; bytes counted at the f16 cache
+    width the GPU streams."""
+    threads = threads or _host_threads()
+    v_all, dt_all, b_all = _decode_sample(w, DECODE_SAMPLE_ALL, threads, reps)
+    v_one, dt_one, b_one = _decode_sample(w, DECODE_SAMPLE_ONE, 1, reps)
+    return {"value": v_all, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"oracle attn_decode on the first {b_all} of {w.B} sequences (f32 math, "
+                      f"bytes counted at f16 cache width), median of {reps}: {dt_all:.2f} s, "
+                      f"{threads} threads",
+            "single_thread": {"value": v_one, "unit": "GB/s", "cores": 1,
+                              "sample": f"the first sequence, median of {reps}: {dt_one:.2f} s"}}
 
 
 # ---------------------------------------------------------------- main
 def run_reference(args):
+    """The reference arm: the reference's CPU implementation of the path (the
+    oracle port; the Rust/wgpu reference cannot run here) on the host cores,
+    each step one timing of the same fixed all-threads sample the bench arm
+    reports, `value` the median over the timed steps."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     w = make_workload(args.workload, args.batch)
-    threads = len(os.sched_getaffinity(0))
-    vals = []
-    base = None
-    fixed = None
-    per_step = min(6.0, 90.0 / max(1, args.steps + args.warmup))
+    threads = _host_threads()
+    if isinstance(w, PrefillWork):
+        one = lambda: cpu_baseline_prefill(w, threads=threads, reps=1)
+    elif isinstance(w, BatchedDecodeWork):
+        one = lambda: cpu_baseline_decode(w, threads=threads, reps=1)
+    elif isinstance(w, LinearWork):
+        one = lambda: cpu_baseline_linear(w, threads=threads, reps=1)
+    else:
+        raise SystemExit("--impl reference supports cfg1, cfg3, cfg3w, cfg4, cfg5, proj3, projd")
+    vals, singles, base = [], [], None
     for i in range(args.warmup + args.steps):
-        if isinstance(w, PrefillWork):
-            # the first call sizes the sample to ~per_step seconds; later steps reuse it
-            b = cpu_baseline_prefill(w, target_s=per_step, threads=threads, sample=fixed)
-            fixed = b["_sample"]
-        elif isinstance(w, BatchedDecodeWork):
-            b = cpu_baseline_decode(w, threads=threads, n_seq=2)
-        elif isinstance(w, LinearWork):
-            b = cpu_baseline_linear(w, threads=threads, target_s=per_step)
-        else:
-            raise SystemExit("--impl reference supports cfg1, cfg3, cfg4, cfg5, proj3, projd")
+        b = one()
         if i >= args.warmup:
             vals.append(b["value"])
+            singles.append(b["single_thread"]["value"])
             base = b
     v = statistics.median(vals)
+    single = dict(base["single_thread"], value=statistics.median(singles))
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": base["unit"],
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "data": "synthetic", "dtype": "f32",
             "config": w.describe(1),
             "cpu_baseline": {"value": v, "unit": base["unit"], "cores": base["cores"],
-                             "kind": "port", "sample": base["sample"]
-                             + f"; median of {args.steps} timed samples"},
+                             "kind": "port", "sample": base["sample"].split("; median")[0]
+                             + f"; median of {args.steps} timed steps",
+                             "single_thread": single},
             "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "note": "reference = oracle/ C restatement of crates/eyebrowse-kernels/src/testutil.rs "
@@ -1006,7 +1078,6 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         if is_prefill:
             cpu = cpu_baseline_prefill(w)
-            cpu.pop("_sample", None)
         elif isinstance(w, BatchedDecodeWork):
             cpu = cpu_baseline_decode(w)
         elif isinstance(w, LinearWork):

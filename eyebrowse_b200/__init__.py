@@ -29,7 +29,7 @@ EXPORTS = (
     "eb_attention_decode", "eb_attention_decode_batched", "eb_attention_decode_workspace_bytes",
     "eb_workspace_init", "eb_head_concat", "eb_get_device_error",
     "eb_attention_decode_noalloc", "eb_head_broadcast", "eb_linear_f16w",
-    "eb_linear_f16w_workspace_bytes",
+    "eb_linear_f16w_workspace_bytes", "eb_selftest_wait_timeout",
 )
 
 
@@ -115,6 +115,7 @@ def lib() -> ctypes.CDLL:
     L.eb_workspace_init.argtypes = [_vp, _sz, _vp]
     L.eb_head_concat.argtypes = [_vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_int32, _vp]
     L.eb_get_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
+    L.eb_selftest_wait_timeout.argtypes = [ctypes.c_uint32, _vp]
     _lib = L
     return L
 
@@ -340,6 +341,17 @@ def device_error() -> int:
     if st not in (0, 6):
         raise EbError(st, "eb_get_device_error")
     return bits.value
+
+
+DEVICE_ERROR_SELFTEST = 1 << 5
+
+
+def selftest_wait_timeout(timeout_us: int, stream=None):
+    """eb_selftest_wait_timeout: a kernel whose bounded wait never completes
+    gives up after timeout_us and sets DEVICE_ERROR_SELFTEST in the device
+    error word (read and cleared by device_error())."""
+    _check(lib().eb_selftest_wait_timeout(timeout_us, _stream(stream)),
+           "eb_selftest_wait_timeout")
 
 
 def alloc_workspace(nbytes: int, device=None):

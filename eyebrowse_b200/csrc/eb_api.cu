@@ -49,6 +49,24 @@ int device_ok() {
   return ok_dev[dev] == 1;
 }
 
+int sm_count() {
+  static int cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148;
+  }
+  int n = __atomic_load_n(&cache[dev], __ATOMIC_RELAXED);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      return 148;
+    }
+    __atomic_store_n(&cache[dev], n, __ATOMIC_RELAXED);
+  }
+  return n;
+}
+
 static int elem_bytes(int dt) { return dt == kF32 ? 4 : 2; }
 static bool dtype_ok(int dt) { return dt == kF32 || dt == kF16 || dt == kBF16; }
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -72,7 +90,8 @@ struct DecodePlan {
 #ifndef EB_DECODE_CTAS_PER_SM
 #define EB_DECODE_CTAS_PER_SM 2
 #endif
-static constexpr int64_t kDecodeTargetCtas = EB_DECODE_CTAS_PER_SM * 148;
+// The split-K plan aims at this many CTAs (a few per SM) per decode launch.
+static int64_t decode_target_ctas() { return (int64_t)EB_DECODE_CTAS_PER_SM * sm_count(); }
 
 // Split-K workspace layout for p.cmax chunks: combine tickets, then the
 // per-chunk (max, sum) pairs, then the per-chunk partial outputs.
@@ -93,7 +112,7 @@ static DecodePlan plan_decode(int64_t batch, int64_t h, int64_t hkv, int64_t hd,
     return p;
   }
   const int rpb = decode_rows_per_batch((int)hd, dtype_cache, (int)(h / hkv));
-  const int64_t target_ctas = kDecodeTargetCtas;
+  const int64_t target_ctas = decode_target_ctas();
   int64_t chunk = (rows * batch * hkv + target_ctas - 1) / target_ctas;
   chunk = (chunk + rpb - 1) / rpb * rpb;
   if (chunk < rpb) chunk = rpb;
@@ -123,7 +142,8 @@ static size_t decode_workspace_bound(int64_t batch, int64_t h, int64_t hkv, int6
   const int64_t rows = max_pos + 1;
   const int64_t rpb = decode_rows_per_batch((int)hd, dtype_cache, (int)(h / hkv));
   const int64_t bh = batch * hkv;
-  int64_t c = (kDecodeTargetCtas + bh - 1) / bh;
+  const int64_t target = decode_target_ctas();
+  int64_t c = (target + bh - 1) / bh;
   c = std::max<int64_t>(c, (rows + 8191) / 8192);
   c = std::min<int64_t>(c, 256);
   c = std::min<int64_t>(c, (rows + rpb - 1) / rpb);
@@ -785,6 +805,15 @@ int eb_head_broadcast(const void* local, void* multicast, int64_t rows, int64_t 
   return cuda_status(launch_head_broadcast(local, multicast, rows, n_heads_total, head_offset,
                                            n_heads, head_dim, es,
                                            reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int eb_selftest_wait_timeout(uint32_t timeout_us, eb_stream_t stream) {
+  if (timeout_us < 1 || timeout_us > 1000000) return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  unsigned* err = error_word_ptr();
+  if (!err) return EB_ERR_CUDA;
+  return cuda_status(launch_wait_timeout_selftest(err, 1000ull * timeout_us,
+                                                  reinterpret_cast<cudaStream_t>(stream)));
 }
 
 int eb_get_device_error(uint32_t* bits) {

@@ -22,6 +22,7 @@ enum : unsigned {
   kErrTimeoutSoftmax = 1u << 2,
   kErrTimeoutEpilogue = 1u << 3,
   kErrTimeoutProducer = 1u << 4,
+  kErrTimeoutSelftest = 1u << 5,  // eb_selftest_wait_timeout's wait (no real kernel failed)
 };
 
 // A bounded wait gives up after this long (device globaltimer, ns). Normal

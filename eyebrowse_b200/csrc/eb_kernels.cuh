@@ -141,10 +141,18 @@ size_t decode_plan_bytes(const eb_attn_desc* d, int64_t batch, int64_t max_pos);
 // device is an sm_100 part.
 bool desc_ok(const eb_attn_desc* d);
 int device_ok();
+// Streaming multiprocessors of the current device (cached per device); 148,
+// a B200's count, when no device is current (host-only calls, e.g. workspace
+// sizing on a machine without a GPU). Grids and split-K plans scale with it.
+int sm_count();
 // Zeroes the split-K tickets of eb_attention_decode_noalloc's scratch on the
 // current device (synchronously); false if a CUDA call failed. Defined in
 // eb_noalloc.cu.
 bool noalloc_clear_tickets();
+// One-CTA kernel whose bounded wait (nothing ever arrives) gives up after
+// timeout_ns and sets kErrTimeoutSelftest in *err. Defined in eb_selftest.cu.
+cudaError_t launch_wait_timeout_selftest(unsigned* err, unsigned long long timeout_ns,
+                                         cudaStream_t st);
 
 // ------------------------------------------------------------- prefill (tcgen05)
 struct PrefillArgs {

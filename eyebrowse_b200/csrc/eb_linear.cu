@@ -331,7 +331,7 @@ cudaError_t launch_linear(const float* x, const void* w, float* y, int64_t m, in
   }
   if (path == LinearPath::kRows) {
     // 4 rows per warp when that still gives two CTAs per SM, else 1
-    const bool wide = out_f >= (int64_t)2 * 148 * kRowsWarps * 4;
+    const bool wide = out_f >= (int64_t)2 * sm_count() * kRowsWarps * 4;
     const int rows_per_cta = kRowsWarps * (wide ? 4 : 1);
     const unsigned grid = (unsigned)((out_f + rows_per_cta - 1) / rows_per_cta);
     const int mi = (int)m, ki = (int)in_f, ni = (int)out_f;
@@ -354,7 +354,7 @@ cudaError_t launch_linear(const float* x, const void* w, float* y, int64_t m, in
   __half* hi = static_cast<__half*>(ws);
   __half* lo = reinterpret_cast<__half*>(static_cast<char*>(ws) + plane);
   const int64_t n8 = m * in_f / 8;
-  split_x_kernel<<<(unsigned)std::min<int64_t>((n8 + 255) / 256, 148 * 16), 256, 0, st>>>(
+  split_x_kernel<<<(unsigned)std::min<int64_t>((n8 + 255) / 256, (int64_t)sm_count() * 16), 256, 0, st>>>(
       x, hi, lo, n8);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

@@ -914,13 +914,8 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* q16, con
   // grid is small (a head-sharded rank with few heads); otherwise the pair
   // wins, its per-head rate being ~1/0.87 of the one-tile kernel's
   // (measured on config 3).
-  static int sms[32] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  int& n_sm = sms[dev & 31];
-  if (n_sm == 0) cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
   const double n_qt = (double)((a.S + 127) / 128);
-  const double per_sm = (double)a.H * n_qt * (n_qt + 1) / 2 / (n_sm > 0 ? n_sm : 148);
+  const double per_sm = (double)a.H * n_qt * (n_qt + 1) / 2 / sm_count();
   const bool pair = ((a.H / a.Hkv) % 2) == 0 &&
                     std::max(2 * n_qt, per_sm) <= std::max(n_qt, per_sm) / 0.87;
   // A contiguous [S][H][hd] output is a one-destination gather: its tiles are

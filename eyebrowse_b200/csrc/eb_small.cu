@@ -71,12 +71,12 @@ cudaError_t launch_kv_write(float* cache, const float* src, int64_t hkv, int64_t
   if ((n % 4) == 0 && (((uintptr_t)dst | (uintptr_t)src) & 15) == 0) {
     const int64_t n4 = n / 4;
     int64_t blocks = (n4 + threads - 1) / threads;
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks > sm_count() * 16) blocks = sm_count() * 16;
     kv_write_kernel_v4<<<(unsigned)blocks, threads, 0, st>>>(
         reinterpret_cast<float4*>(dst), reinterpret_cast<const float4*>(src), n4);
   } else {
     int64_t blocks = (n + threads - 1) / threads;
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks > sm_count() * 16) blocks = sm_count() * 16;
     kv_write_kernel<<<(unsigned)blocks, threads, 0, st>>>(cache, src, n, off);
   }
   return cudaGetLastError();
@@ -135,7 +135,7 @@ cudaError_t launch_head_concat(const void* src, void* dst, int64_t shards, int64
   const int threads = 256;
   auto blocks_for = [&](int64_t n) {
     int64_t b = (n + threads - 1) / threads;
-    return (unsigned)(b > 148 * 32 ? 148 * 32 : b);
+    return (unsigned)(b > (int64_t)sm_count() * 32 ? (int64_t)sm_count() * 32 : b);
   };
   if (row_bytes % 16 == 0 && (((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
     const int64_t ru = row_bytes / 16;
@@ -179,7 +179,7 @@ cudaError_t launch_head_broadcast(const void* local, void* mc, int64_t rows, int
   const int64_t total = rows * span16;
   const int threads = 512;
   int64_t blocks = (total + threads - 1) / threads;
-  if (blocks > 148 * 4) blocks = 148 * 4;
+  if (blocks > sm_count() * 4) blocks = sm_count() * 4;
   head_broadcast_kernel<<<(unsigned)blocks, threads, 0, st>>>(
       static_cast<const char*>(local), static_cast<char*>(mc), rows, h_total * hd * elem_bytes,
       h0 * hd * elem_bytes, span16);

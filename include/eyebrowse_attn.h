@@ -305,6 +305,15 @@ EB_API int eb_head_broadcast(const void* local, void* multicast, int64_t rows,
  * needs eb_workspace_init again.) */
 EB_API int eb_get_device_error(uint32_t* bits);
 
+/* Checks the failure path of the kernels' bounded waits on this device: a
+ * one-CTA kernel waits on a barrier that nothing completes, gives up after
+ * timeout_us microseconds (1 .. 1e6), sets bit EB_DEVICE_ERROR_SELFTEST in
+ * the device error word and returns. No fault, no hang: the context stays
+ * usable, and eb_get_device_error then reports (and clears) the bit. No
+ * counterpart in the reference (its kernels have no waits). */
+#define EB_DEVICE_ERROR_SELFTEST (1u << 5)
+EB_API int eb_selftest_wait_timeout(uint32_t timeout_us, eb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
