@@ -33,7 +33,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from eyebrowse_b200.sharded import GatheredOutput, gather_heads, head_shard  # noqa: E402
+from eyebrowse_b200.sharded import (GatheredOutput, decode_shard, gather_heads,  # noqa: E402
+                                    head_shard)
 
 METRIC = "prefill attn TFLOP/s & decode KV GB/s at 1/2/4/8 B200 vs roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -435,7 +436,12 @@ class PrefillWork:
 
 
 class BatchedDecodeWork:
-    """Config 5: batched decode, KV heads sharded over ranks."""
+    """Config 5: batched decode. On N GPUs each rank owns a KV-head group of a
+    context-balanced bucket of the sequences (eyebrowse_b200.sharded.
+    decode_shard: the head split first, the sequences over the rest) and its
+    kernel stores the output rows into every rank's gathered [B, H, hd]
+    buffer over NVLink (--gather nccl: head split only, NCCL all-gather +
+    eb_head_concat)."""
 
     def __init__(self, name="cfg5", B=64, H=32, Hkv=8, hd=128, max_seq=32768, ctx_lo=512,
                  ctx_hi=32768, theta=5e5, dt=1, seed=5):
@@ -446,17 +452,27 @@ class BatchedDecodeWork:
         self.pos = (self.ctx - 1).astype(np.int32)
 
     def describe(self, world):
+        sh = getattr(self, "sh", None)
+        par = "1 GPU"
+        if world > 1 and sh is not None:
+            par = f"kv-heads/{sh.head_groups} x sequences/{world // sh.head_groups}"
         return {"workload": self.name, "batch": self.B, "n_heads": self.H, "n_kv_heads": self.Hkv,
                 "head_dim": self.hd, "max_seq": self.max_seq, "ctx_sum": int(self.ctx.sum()),
-                "ctx_range": [int(self.ctx.min()), int(self.ctx.max())],
-                "parallelism": f"kv-heads/{world}" if world > 1 else "1 GPU"}
+                "ctx_range": [int(self.ctx.min()), int(self.ctx.max())], "parallelism": par,
+                "head_concat": None if world == 1 else (
+                    "NCCL all-gather + eb_head_concat" if GATHER != "fused" else
+                    "fused: the decode kernel stores its rows into every rank's buffer")}
+
+    def _bytes(self, seqs, hkv, h):
+        es = 2 if self.dt != 0 else 4
+        n = len(seqs)
+        kv_rows = 2.0 * self.ctx[list(seqs)].sum() * hkv * self.hd * es  # cache rows read (incl. new)
+        new_kv = 2.0 * n * hkv * self.hd * es * 2                          # new k/v read + written
+        qo = n * h * self.hd * es * 2                                      # q read, o written
+        return kv_rows + new_kv + qo
 
     def bytes_total(self) -> float:
-        es = 2 if self.dt != 0 else 4
-        kv_rows = 2.0 * self.ctx.sum() * self.Hkv * self.hd * es   # cache rows read (incl. new)
-        new_kv = 2.0 * self.B * self.Hkv * self.hd * es * 2          # new k/v read + written
-        qo = self.B * self.H * self.hd * es * 2                      # q read, o written
-        return kv_rows + new_kv + qo
+        return self._bytes(range(self.B), self.Hkv, self.H)
 
     def setup(self, rank, world):
         import torch
@@ -464,50 +480,79 @@ class BatchedDecodeWork:
         import eyebrowse_b200 as eb
         self.eb = eb
         self.world = world
-        sh = head_shard(self.H, self.Hkv, world, rank)
-        self.Hl, self.Hkvl = sh.n_heads, sh.n_kv_heads
+        if world > 1 and GATHER != "fused":
+            self.sh = decode_shard(self.H, self.Hkv, world, rank, self.ctx, head_groups=world)
+        else:
+            self.sh = decode_shard(self.H, self.Hkv, world, rank, self.ctx)
+        sh = self.sh
+        self.seqs = list(sh.seqs)
+        self.Bl, self.Hl, self.Hkvl = len(self.seqs), sh.n_heads, sh.n_kv_heads
         tdt = {0: torch.float32, 1: torch.float16, 2: torch.bfloat16}[self.dt]
         self.tdt = tdt
         g = torch.Generator(device="cuda").manual_seed(self.seed * 1000 + rank)
-        B, hd = self.B, self.hd
-        self.kc = torch.randn(B, self.max_seq, self.Hkvl, hd, device="cuda", generator=g).to(tdt)
-        self.vc = torch.randn(B, self.max_seq, self.Hkvl, hd, device="cuda", generator=g).to(tdt)
-        self.q = torch.randn(B, self.Hl, hd, device="cuda", generator=g).to(tdt)
-        self.k = torch.randn(B, self.Hkvl, hd, device="cuda", generator=g).to(tdt)
-        self.v = torch.randn(B, self.Hkvl, hd, device="cuda", generator=g).to(tdt)
-        self.o = torch.empty(B, self.Hl, hd, device="cuda", dtype=tdt)
-        self.posd = torch.from_numpy(self.pos).cuda()
+        Bl, hd = self.Bl, self.hd
+        self.kc = torch.randn(Bl, self.max_seq, self.Hkvl, hd, device="cuda", generator=g).to(tdt)
+        self.vc = torch.randn(Bl, self.max_seq, self.Hkvl, hd, device="cuda", generator=g).to(tdt)
+        self.q = torch.randn(Bl, self.Hl, hd, device="cuda", generator=g).to(tdt)
+        self.k = torch.randn(Bl, self.Hkvl, hd, device="cuda", generator=g).to(tdt)
+        self.v = torch.randn(Bl, self.Hkvl, hd, device="cuda", generator=g).to(tdt)
+        self.o = torch.empty(Bl, self.Hl, hd, device="cuda", dtype=tdt)
+        lpos = self.pos[self.seqs]
+        self.posd = torch.from_numpy(np.ascontiguousarray(lpos)).cuda()
+        self.seq_idx = torch.tensor(self.seqs, dtype=torch.int32, device="cuda")
         cos, sin = eb.rope_tables(self.max_seq, hd, self.theta)
         self.cos = torch.from_numpy(cos).cuda()
         self.sin = torch.from_numpy(sin).cuda()
         self.desc = eb.make_desc(self.Hl, self.Hkvl, hd, self.max_seq, dtype_qkv=self.dt,
                                  dtype_cache=self.dt, dtype_out=self.dt)
         self.layer = eb.make_layer(rope_cos=self.cos, rope_sin=self.sin)
-        self.max_pos = int(self.pos.max())
-        nb = eb.attention_decode_workspace_bytes(self.desc, B, self.max_pos)
+        self.max_pos = int(lpos.max())
+        nb = eb.attention_decode_workspace_bytes(self.desc, Bl, self.max_pos)
         self.ws = eb.alloc_workspace(nb) if nb else None
-        if world > 1:
-            self.gath = torch.empty(world, B, self.Hl, hd, device="cuda", dtype=tdt)
-            self.full = torch.empty(B, self.H, hd, device="cuda", dtype=tdt)
+        self.gout = None
+        if world > 1 and GATHER == "fused":
+            self.gout = GatheredOutput(self.B, self.H, hd, tdt, sh)
+            self.full = self.gout.bufs[0]
+            self.launches_per_step = 2  # decode (with the peer stores), barrier
+        elif world > 1:
+            self.gath = torch.empty(world, self.B, self.Hl, hd, device="cuda", dtype=tdt)
+            self.full = torch.empty(self.B, self.H, hd, device="cuda", dtype=tdt)
+            self.launches_per_step = 2  # decode, head concat (plus NCCL's all-gather)
         else:
             self.full = self.o
-        self.launches_per_step = 1 + (1 if world > 1 else 0)
+            self.launches_per_step = 1
+
+    def _call(self, gather=None):
+        if gather is None:
+            self.eb.attention_decode_batched(self.desc, self.layer, self.Bl, self.posd,
+                                             self.max_pos, self.q, self.k, self.v, self.kc,
+                                             self.vc, self.max_seq * self.Hkvl * self.hd, self.o,
+                                             self.ws)
+        else:
+            self.eb.attention_decode_batched_gather(
+                self.desc, self.layer, self.Bl, self.posd, self.max_pos, self.q, self.k, self.v,
+                self.kc, self.vc, self.max_seq * self.Hkvl * self.hd, gather, self.seq_idx,
+                self.ws)
 
     def step(self):
-        self.eb.attention_decode_batched(self.desc, self.layer, self.B, self.posd, self.max_pos,
-                                         self.q, self.k, self.v, self.kc, self.vc,
-                                         self.max_seq * self.Hkvl * self.hd, self.o, self.ws)
+        if self.gout is not None:
+            self._call(self.gout.next())
+            self.gout.finish()
+            self.full = self.gout.full
+            return
+        self._call()
         if self.world > 1:
             gather_heads(self.o, self.gath, self.full, self.world, self.B, self.Hl, self.hd,
                          self.dt)
 
     def kernel_only(self):
-        self.eb.attention_decode_batched(self.desc, self.layer, self.B, self.posd, self.max_pos,
-                                         self.q, self.k, self.v, self.kc, self.vc,
-                                         self.max_seq * self.Hkvl * self.hd, self.o, self.ws)
+        """The decode kernel alone (with its NVLink stores when fused; calls
+        back to back store the same values into this rank's rows, so no
+        barrier is needed between them)."""
+        self._call(self.gout.gathers[0] if self.gout is not None else None)
 
     def kernel_units(self):
-        return self.bytes_total() / self.world
+        return self._bytes(self.seqs, self.Hkvl, self.Hl)
 
 
 class DecodeWork:

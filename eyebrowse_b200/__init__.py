@@ -30,6 +30,7 @@ EXPORTS = (
     "eb_workspace_init", "eb_head_concat", "eb_get_device_error",
     "eb_attention_decode_noalloc", "eb_head_broadcast", "eb_linear_f16w",
     "eb_linear_f16w_workspace_bytes", "eb_selftest_wait_timeout",
+    "eb_attention_decode_batched_gather",
 )
 
 
@@ -109,6 +110,8 @@ def lib() -> ctypes.CDLL:
     L.eb_attention_decode.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]
     L.eb_attention_decode_batched.argtypes = [dp, lp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp,
                                               _i64, _vp, _vp, _sz, _vp]
+    L.eb_attention_decode_batched_gather.argtypes = [dp, lp, _i64, _vp, _i64, _vp, _vp, _vp, _vp,
+                                                     _vp, _i64, gp, _vp, _vp, _sz, _vp]
     L.eb_attention_decode_workspace_bytes.restype = _sz
     L.eb_attention_decode_workspace_bytes.argtypes = [dp, _i64, _i64]
     L.eb_attention_decode_noalloc.argtypes = [dp, lp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
@@ -312,6 +315,20 @@ def attention_decode_batched(desc, layer, batch, positions, max_pos, q, k, v, kc
                                              _ptr(kcache), _ptr(vcache), cache_batch_stride,
                                              _ptr(o), _ptr(workspace), ws_bytes, _stream(stream)),
            "eb_attention_decode_batched")
+
+
+def attention_decode_batched_gather(desc, layer, batch, positions, max_pos, q, k, v, kcache,
+                                    vcache, cache_batch_stride, gather: HeadGather,
+                                    seq_index=None, workspace=None, stream=None):
+    """eb_attention_decode_batched_gather: batched decode whose kernel stores
+    each output row into every rank's gathered buffer (row seq_index[b] or b,
+    heads gather.head_offset + h) instead of o."""
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _check(lib().eb_attention_decode_batched_gather(
+        ctypes.byref(desc), ctypes.byref(layer), batch, _ptr(positions), max_pos, _ptr(q),
+        _ptr(k), _ptr(v), _ptr(kcache), _ptr(vcache), cache_batch_stride, ctypes.byref(gather),
+        _ptr(seq_index), _ptr(workspace), ws_bytes, _stream(stream)),
+        "eb_attention_decode_batched_gather")
 
 
 def attention_decode_noalloc(desc, layer, pos, q, k, v, kcache, vcache, o, stream=None):

@@ -185,12 +185,36 @@ size_t decode_plan_bytes(const eb_attn_desc* d, int64_t batch, int64_t max_pos) 
       .bytes;
 }
 
+// Chunks per (sequence, KV-head group) of the cluster-combined decode, or 0
+// when the workspace kernels serve the call: 16-bit f16 caches take the
+// tensor-core kernel, and the cluster kernel is used only when its grid is
+// one wave (one CTA per SM, every cluster resident at once) with whole-batch
+// chunks -- the latency case of a single sequence or a few. At most 16 CTAs
+// per cluster.
+static int cl_chunks(const eb_attn_desc* d, int64_t batch, int64_t span_pos) {
+  const int group = d->n_heads / d->n_kv_heads;
+  if (!decode_cl_supported(d->head_dim, d->dtype_cache) ||
+      decode_tc_supported(d->head_dim, d->dtype_cache, group))
+    return 0;
+  const int gs = group % 8 == 0 ? 8 : group % 4 == 0 ? 4 : group % 2 == 0 ? 2 : 1;
+  const int64_t groups = (int64_t)d->n_kv_heads * (group / gs) * batch;
+  const int64_t rpb = decode_cl_rows_per_batch(d->head_dim, d->dtype_cache, group);
+  const int64_t want = std::min<int64_t>(16, (span_pos + 1 + rpb - 1) / rpb);
+  const int64_t fit = sm_count() / groups;
+  // every cluster resident at once (a second wave would double the latency)
+  const int64_t res = decode_cl_cluster_limit(d->head_dim, d->dtype_cache, group, groups);
+  const int64_t n = std::min(std::min(want, fit), res);
+  if (n < 1 || (n < want && n < 4)) return 0;
+  return (int)n;
+}
+
 // Shared body of single and batched decode (also used by eb_noalloc.cu).
 int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
                        const int32_t* positions, int64_t pos_scalar, int64_t max_pos,
                        const void* q, const void* k, const void* v, void* kc, void* vc,
                        int64_t cache_bstride, void* o, int64_t q_bstride, int64_t kv_bstride,
-                       int64_t o_bstride, void* ws, size_t ws_bytes, cudaStream_t st) {
+                       int64_t o_bstride, void* ws, size_t ws_bytes, cudaStream_t st,
+                       const GatherSpec* gather, const int32_t* seq_idx) {
   const int hd = d->head_dim;
   const float* cos_t = L ? L->rope_cos : nullptr;
   const float* sin_t = L ? L->rope_sin : nullptr;
@@ -198,6 +222,10 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
   const int64_t span_pos = attended_max_pos(d, max_pos);
   DecodePlan p = plan_decode(batch, d->n_heads, d->n_kv_heads, hd, d->dtype_cache, span_pos);
   const bool vec = (hd == 64 || hd == 128 || hd == 256);
+  // One wave for the whole context (a single sequence or a few): the
+  // cluster-combined kernel, no workspace (see cl_chunks).
+  const int n_cl = vec ? cl_chunks(d, batch, span_pos) : 0;
+  if (n_cl > 0) p.cmax = 1;
   if (vec && p.cmax > 1 && (ws == nullptr || ws_bytes < p.bytes)) {
     if (ws != nullptr && ws_bytes != 0) return EB_ERR_WORKSPACE;
     p.chunk = (int)(span_pos + 1);  // no workspace: one CTA walks the whole context
@@ -248,11 +276,24 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
       a.ws_ml = reinterpret_cast<float*>(w + p.ml_off);
       a.ws_acc = reinterpret_cast<float*>(w + p.acc_off);
     }
+    if (gather) {
+      a.n_dst = gather->n_dst;
+      a.dst_h_off = gather->h_off;
+      a.dst_bstride = gather->n_heads_total * hd;
+      a.seq_idx = seq_idx;
+      for (int i = 0; i < gather->n_dst; i++) a.dst[i] = gather->dst[i];
+    }
     a.err = error_word_ptr();
     if (!a.err) return EB_ERR_CUDA;
+    if (n_cl > 0) {
+      a.chunk = (int)((span_pos + 1 + n_cl - 1) / n_cl);
+      a.cmax = n_cl;
+      return cuda_status(launch_decode_cl(a, d->dtype_cache, (int)batch, n_cl, st));
+    }
     return cuda_status(launch_decode(a, d->dtype_cache, (int)batch, st));
   }
   // SIMT path: K/V prep writes the cache row, then attention over the cache.
+  if (gather) return EB_ERR_INVALID_ARGUMENT;  // head gathers need head_dim 64/128/256
   if (k) {
     PrepArgs pa{};
     pa.k = k;
@@ -775,6 +816,31 @@ int eb_attention_decode_batched(const eb_attn_desc* d, const eb_attn_layer* L, i
                      cache_batch_stride, o, qs_of(d), kvs_of(d), os_of(d), workspace,
                      workspace_bytes,
                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+int eb_attention_decode_batched_gather(const eb_attn_desc* d, const eb_attn_layer* L,
+                                       int64_t batch, const int32_t* positions, int64_t max_pos,
+                                       const void* q, const void* k, const void* v, void* kcache,
+                                       void* vcache, int64_t cache_batch_stride,
+                                       const eb_head_gather* g, const int32_t* seq_index,
+                                       void* workspace, size_t workspace_bytes,
+                                       eb_stream_t stream) {
+  if (!desc_ok(d) || batch < 0 || max_pos < 0 || max_pos >= d->max_seq)
+    return EB_ERR_INVALID_ARGUMENT;
+  if (!g || g->n_dst < 1 || g->n_dst > kMaxGather || g->head_offset < 0 ||
+      g->n_heads_total < 1 || (int64_t)g->head_offset + d->n_heads > g->n_heads_total || !g->dst)
+    return EB_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < g->n_dst; i++)
+    if (!g->dst[i] || (g->dst[i] & 15)) return EB_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return EB_OK;
+  if (!positions || !q || !k || !v || !kcache || !vcache) return EB_ERR_INVALID_ARGUMENT;
+  if (cache_batch_stride < (int64_t)d->max_seq * d->n_kv_heads * d->head_dim)
+    return EB_ERR_INVALID_ARGUMENT;
+  if (!device_ok()) return EB_ERR_NO_DEVICE;
+  GatherSpec gs{g->n_dst, g->head_offset, g->n_heads_total, g->dst};
+  return decode_impl(d, L, batch, positions, 0, max_pos, q, k, v, kcache, vcache,
+                     cache_batch_stride, nullptr, qs_of(d), kvs_of(d), 0, workspace,
+                     workspace_bytes, reinterpret_cast<cudaStream_t>(stream), &gs, seq_index);
 }
 
 int eb_workspace_init(void* workspace, size_t workspace_bytes, eb_stream_t stream) {

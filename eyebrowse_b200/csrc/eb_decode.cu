@@ -15,6 +15,7 @@
 // resets the ticket counter to zero for the next call.
 #include "eb_common.cuh"
 #include "eb_kernels.cuh"
+#include "eb_decode_out.cuh"
 #include "eb_rowops.cuh"
 
 namespace eb {
@@ -236,7 +237,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
       if (sm_m[s2][g] != -INFINITY) O += sacc[(s2 * G + g) * HD + d] * ex2(sm_m[s2][g] - M);
     const int h = head0 + g;
     if (!split) {
-      st_any(a.o, (int64_t)b * a.o_bstride + (int64_t)h * HD + d, a.dtype_o, O / sm_L[g]);
+      dec_store(a, b, h, HD, d, O / sm_L[g]);
     } else {
       a.ws_acc[(((int64_t)b * a.H + h) * a.cmax + c) * HD + d] = O;
     }
@@ -288,7 +289,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_kernel(DecodeArgs a, in
     }
     for (; cc < n_chunks; cc++) O8[0] += __ldcg(pa + (int64_t)cc * HD) * wg[cc];
     const float O = ((O8[0] + O8[1]) + (O8[2] + O8[3])) + ((O8[4] + O8[5]) + (O8[6] + O8[7]));
-    st_any(a.o, (int64_t)b * a.o_bstride + (int64_t)h * HD + d, a.dtype_o, O / sm_L[g]);
+    dec_store(a, b, h, HD, d, O / sm_L[g]);
   }
   if (tid == 0) *cnt = 0u;
 }

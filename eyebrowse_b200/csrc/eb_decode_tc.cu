@@ -22,6 +22,7 @@
 #include <type_traits>
 
 #include "eb_common.cuh"
+#include "eb_decode_out.cuh"
 #include "eb_kernels.cuh"
 #include "eb_rowops.cuh"
 #include "eb_tc.cuh"
@@ -407,9 +408,10 @@ __global__ void __launch_bounds__(96)
               dst[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
                                    __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
           } else {
-            const int64_t ob = (int64_t)b * a.o_bstride + (int64_t)h * HD + cc * 32;
+            float ov[32];
 #pragma unroll
-            for (int i = 0; i < 32; i++) st_any(a.o, ob + i, a.dtype_o, __uint_as_float(o[i]) * inv_l);
+            for (int i = 0; i < 32; i++) ov[i] = __uint_as_float(o[i]) * inv_l;
+            dec_store32(a, b, h, HD, cc * 32, ov);
           }
         }
       }
@@ -457,7 +459,7 @@ __global__ void __launch_bounds__(96)
               }
               for (; k < n_chunks; k++) O8[0] += __ldcg(accg + (int64_t)k * HD + d) * wts[k];
               const float O = ((O8[0] + O8[1]) + (O8[2] + O8[3])) + ((O8[4] + O8[5]) + (O8[6] + O8[7]));
-              st_any(a.o, (int64_t)b * a.o_bstride + (int64_t)hh * HD + d, a.dtype_o, O / L);
+              dec_store(a, b, hh, HD, d, O / L);
             }
             __syncwarp();  // wts is rewritten for the next head
           }

@@ -9,6 +9,10 @@
 
 namespace eb {
 
+// Destinations of a head gather (prefill and decode): at most this many
+// buffers, this GPU's and its peers'.
+constexpr int kMaxGather = 8;
+
 // ------------------------------------------------------------- small kernels
 cudaError_t launch_rope(const float* x, const float* cos_t, const float* sin_t, float* out,
                         int64_t seq, int64_t n_heads, int64_t hd, int64_t base_pos,
@@ -107,6 +111,15 @@ struct DecodeArgs {
   float* ws_acc;       // [B][H][cmax][hd]
   unsigned* ws_cnt;    // [B][Hkv] tickets
   unsigned* err;
+  // Head gather (n_dst > 0): instead of o, sequence b's rows go to row
+  // seq_idx[b] (b if null), heads dst_h_off + h, of every buffer dst[i]
+  // [rows][heads][hd] in dtype_o, dst_bstride elements per row
+  // (eb_decode_out.cuh).
+  int n_dst;
+  int dst_h_off;
+  int64_t dst_bstride;
+  const int32_t* seq_idx;
+  uint64_t dst[kMaxGather];
 };
 // Returns cudaErrorNotSupported when (hd, cache dtype) has no vector kernel.
 cudaError_t launch_decode(const DecodeArgs& a, int dtype_cache, int batch, cudaStream_t st);
@@ -123,6 +136,16 @@ cudaError_t launch_linear(const float* x, const void* w, float* y, int64_t m, in
                           int64_t out_f, void* ws, LinearPath path, unsigned* err,
                           cudaStream_t st);
 
+// Latency decode for f32/bf16 caches (eb_decode_cl.cu): n_chunks (1..16)
+// CTAs per (sequence, KV-head group) form a cluster and merge through
+// distributed shared memory; no workspace. a.chunk = rows per CTA.
+bool decode_cl_supported(int hd, int dtype_cache);
+int decode_cl_rows_per_batch(int hd, int dtype_cache, int group);
+// The largest cluster size (16, 8, 4, 2, 1; 0 if none) at which `clusters`
+// clusters of the latency decode kernel are all resident at once.
+int decode_cl_cluster_limit(int hd, int dtype_cache, int group, int64_t clusters);
+cudaError_t launch_decode_cl(const DecodeArgs& a, int dtype_cache, int batch, int n_chunks,
+                             cudaStream_t st);
 // tcgen05 decode for 16-bit caches (eb_decode_tc.cu)
 bool decode_tc_supported(int hd, int dtype_cache, int group);
 cudaError_t launch_decode_tc(const DecodeArgs& a, int dtype_cache, int batch, cudaStream_t st);
@@ -132,7 +155,8 @@ int decode_impl(const eb_attn_desc* d, const eb_attn_layer* L, int64_t batch,
                 const int32_t* positions, int64_t pos_scalar, int64_t max_pos, const void* q,
                 const void* k, const void* v, void* kc, void* vc, int64_t cache_bstride, void* o,
                 int64_t q_bstride, int64_t kv_bstride, int64_t o_bstride, void* ws, size_t ws_bytes,
-                cudaStream_t st);
+                cudaStream_t st, const struct GatherSpec* gather = nullptr,
+                const int32_t* seq_idx = nullptr);
 // Workspace bytes the split-K plan of one decode call at max_pos needs (0 when
 // it does not split), defined in eb_api.cu.
 size_t decode_plan_bytes(const eb_attn_desc* d, int64_t batch, int64_t max_pos);
@@ -183,7 +207,6 @@ struct PrefillArgs {
 };
 // Destinations of a head gather: up to kMaxGather buffers [S][H_total][hd]
 // in the output dtype (this GPU's and its peers', mapped here).
-constexpr int kMaxGather = 8;
 struct GatherSpec {
   int n_dst;
   int h_off;

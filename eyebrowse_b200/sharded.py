@@ -1,19 +1,28 @@
-"""Head-sharded attention across GPUs: one process per GPU, torch.distributed
+"""Sharded attention across GPUs: one process per GPU, torch.distributed
 for the plumbing, and a single exchange at the head-concat boundary.
 
-Attention is independent per KV-head group, so rank g of G owns KV heads
-[g*Hkv/G, (g+1)*Hkv/G) and their query heads, keeps its own cache slice
-[max_seq, Hkv/G, hd] and runs the fused call on its slice with no traffic to
-other ranks. The per-rank outputs [rows, H/G, hd] meet at the head-concat
-boundary in one of two ways:
-  - GatheredOutput + eb_attention_prefill_gather: the attention kernel stores
-    every finished output tile straight into every rank's [rows, H, hd]
-    buffer over NVLink (TMA stores into peer memory) while the rest of the
-    kernel runs; or, from 8 GPUs, it writes its own buffer and
-    eb_head_broadcast sends its heads once through an NVLink multicast
-    address. No library collective runs.
+Attention is independent per KV-head group and per sequence:
+  - prefill (head_shard): rank g of G owns KV heads [g*Hkv/G, (g+1)*Hkv/G)
+    and their query heads, keeps its own cache slice [max_seq, Hkv/G, hd]
+    and runs the fused call on its slice with no traffic to other ranks;
+  - batched decode (decode_shard): the ranks form a grid of KV-head groups x
+    sequence buckets -- the head split first (as many groups as divide both
+    the world and Hkv), the sequences of a decode batch spread over the rest
+    and balanced by context length -- so a model with fewer KV heads than
+    GPUs still uses every GPU.
+The per-rank outputs meet at the head-concat boundary in one of two ways:
+  - GatheredOutput: the attention kernel itself stores every finished output
+    tile or row into every rank's gathered buffer over NVLink (TMA stores for
+    prefill, eb_attention_prefill_gather; plain stores for decode,
+    eb_attention_decode_batched_gather) while the rest of the kernel runs.
+    No library collective runs; one device barrier per step.
   - gather_heads: NCCL all-gather into [G, rows, H/G, hd], then
-    eb_head_concat restores [rows, H, hd] (the library-collective baseline).
+    eb_head_concat restores [rows, H, hd] (the library-collective baseline,
+    head split only).
+GatheredOutput also keeps a multicast mode for prefill (one store through
+the NVLink multicast address, eb_head_broadcast): bit-identical, but slower
+on this B200 pool at 8 GPUs (its docstring has the figures); "auto" picks
+the peer stores.
 """
 from __future__ import annotations
 
@@ -52,6 +61,60 @@ def head_shard(n_heads: int, n_kv_heads: int, world: int, rank: int) -> HeadShar
     group = n_heads // n_kv_heads
     kv0 = rank * kv_per
     return HeadShard(rank, world, kv0 * group, (kv0 + kv_per) * group, kv0, kv0 + kv_per)
+
+
+@dataclass(frozen=True)
+class DecodeShard:
+    """A rank's part of a batched decode: query/KV heads [h0, h1) / [kv0, kv1)
+    of the sequences `seqs` (global indices, ascending)."""
+    rank: int
+    world: int
+    head_groups: int
+    h0: int
+    h1: int
+    kv0: int
+    kv1: int
+    seqs: tuple
+
+    @property
+    def n_heads(self) -> int:
+        return self.h1 - self.h0
+
+    @property
+    def n_kv_heads(self) -> int:
+        return self.kv1 - self.kv0
+
+
+def balance_sequences(ctx, buckets: int):
+    """Sequences (indices into ctx) per bucket: longest first, each to the
+    least-loaded bucket (ties to the lowest index), so the K/V rows each
+    bucket reads are balanced. Deterministic: every rank computes the same."""
+    import heapq
+    order = sorted(range(len(ctx)), key=lambda i: (-int(ctx[i]), i))
+    heap = [(0, b) for b in range(buckets)]
+    out = [[] for _ in range(buckets)]
+    for i in order:
+        load, b = heapq.heappop(heap)
+        out[b].append(i)
+        heapq.heappush(heap, (load + int(ctx[i]), b))
+    return [tuple(sorted(x)) for x in out]
+
+
+def decode_shard(n_heads: int, n_kv_heads: int, world: int, rank: int, ctx,
+                 head_groups: int | None = None) -> DecodeShard:
+    """Rank `rank`'s part of a batched decode over sequences with context
+    lengths `ctx`: head group rank % G_h (G_h = head_groups, by default the
+    largest count dividing both world and n_kv_heads) of the sequences in
+    bucket rank // G_h of the world / G_h context-balanced buckets."""
+    import math
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of world {world}")
+    gh = head_groups or math.gcd(world, n_kv_heads)
+    if world % gh or n_kv_heads % gh:
+        raise ValueError(f"{gh} head groups for {world} ranks and {n_kv_heads} KV heads")
+    hs = head_shard(n_heads, n_kv_heads, gh, rank % gh)
+    buckets = balance_sequences(ctx, world // gh)
+    return DecodeShard(rank, world, gh, hs.h0, hs.h1, hs.kv0, hs.kv1, buckets[rank // gh])
 
 
 def gather_heads(o_local, gath, full, world: int, rows: int, heads_per: int, head_dim: int,

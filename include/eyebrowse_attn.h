@@ -241,6 +241,28 @@ EB_API int eb_attention_decode_batched(const eb_attn_desc* desc, const eb_attn_l
                                 void* vcache, int64_t cache_batch_stride, void* o,
                                 void* workspace, size_t workspace_bytes, eb_stream_t stream);
 
+/* Batched decode of a multi-GPU shard with the gather fused into the kernel:
+ * instead of writing o, the kernel stores each finished output row (head h
+ * of local sequence b) into every rank's gathered buffer [rows,
+ * n_heads_total, head_dim] (dtype_out) at row seq_index[b] (b when seq_index
+ * is NULL; a DEVICE array of int32 below that buffer's row count) and head
+ * head_offset + h -- plain stores over NVLink into the peers' buffers, so no
+ * all-gather and no concat follow. The gather's dst and head_offset mean
+ * what they mean for eb_attention_prefill_gather, and the same barriers
+ * apply: nothing else writes the buffers during the call, and every rank's
+ * reads of a buffer are ordered around every rank's call. Head dims other
+ * than 64/128/256 are not supported here (EB_ERR_INVALID_ARGUMENT). Other
+ * arguments as eb_attention_decode_batched. No reference counterpart: it is
+ * the multi-GPU split of batched decode by KV-head group and by sequence. */
+EB_API int eb_attention_decode_batched_gather(const eb_attn_desc* desc, const eb_attn_layer* layer,
+                                              int64_t batch, const int32_t* positions,
+                                              int64_t max_pos, const void* q, const void* k,
+                                              const void* v, void* kcache, void* vcache,
+                                              int64_t cache_batch_stride,
+                                              const eb_head_gather* gather,
+                                              const int32_t* seq_index, void* workspace,
+                                              size_t workspace_bytes, eb_stream_t stream);
+
 /* Workspace for eb_attention_decode(_batched) with contexts up to max_pos+1
  * rows: one workspace of this size serves every call with pos (or the
  * batched max_pos) <= max_pos. 0 means no such call needs one. */
