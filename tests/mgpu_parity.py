@@ -11,8 +11,13 @@ prefill then runs again with the gather fused into the attention kernel
 (eb_attention_prefill_gather: TMA stores into every rank's symmetric-memory
 buffer), and with own-buffer writes followed by eb_head_broadcast through
 the NVLink multicast address; every rank checks that its gathered copy
-equals the NCCL result bit for bit. Exits non-zero on
-any mismatch. Not collected by pytest: it needs N processes.
+equals the NCCL result bit for bit. The batched decode runs the same way,
+then with the gather fused into the decode kernel
+(eb_attention_decode_batched_gather): split by KV-head group it must equal
+the NCCL result bit for bit, split by sequence (eyebrowse_b200.sharded.
+decode_shard with one head group) it is checked against the oracle. Exits
+non-zero on any mismatch. tests/test_gpu_multi.py runs it on 2 GPUs when a
+machine has them.
 """
 import datetime
 import os
@@ -29,7 +34,8 @@ def main() -> int:
     import torch.distributed as dist
 
     import eyebrowse_b200 as eb
-    from eyebrowse_b200.sharded import GatheredOutput, gather_heads, head_shard
+    from eyebrowse_b200.sharded import (GatheredOutput, decode_shard, gather_heads,
+                                        head_shard)
     from oracle import oracle as orc
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -131,6 +137,47 @@ def main() -> int:
         print(f"[mgpu] world={world} batched decode {B} seqs: max_abs={ma:.2e} rel_l2={rl:.2e}",
               flush=True)
         ok &= ma <= 2e-3 and rl <= 1e-3
+    # ---- the same decode with the gather fused into the decode kernel (its
+    # output rows stored into every rank's symmetric-memory buffer): by KV-head
+    # group (bit-identical to the NCCL gather: same per-rank work), and by
+    # sequence only (every rank all heads of a context-balanced bucket of the
+    # sequences; checked against the oracle on rank 0)
+    for head_groups in (None, 1):
+        dsh = decode_shard(H, Hkv, world, rank, pos + 1, head_groups=head_groups)
+        seqs = list(dsh.seqs)
+        ddesc = eb.make_desc(dsh.n_heads, dsh.n_kv_heads, hd, max_seq, dtype_qkv=eb.EB_F16,
+                             dtype_cache=eb.EB_F16, dtype_out=eb.EB_F16)
+        g = GatheredOutput(B, H, hd, f16, dsh)
+        g.bufs.fill_(float("nan"))
+        g.barrier()
+        lpos = pos[seqs]
+        mp = int(lpos.max()) if seqs else 0
+        wsg = eb.alloc_workspace(eb.attention_decode_workspace_bytes(ddesc, max(1, len(seqs)), mp))
+        args = (dev(qd[seqs][:, dsh.h0:dsh.h1]), dev(kd[seqs][:, dsh.kv0:dsh.kv1]),
+                dev(vd[seqs][:, dsh.kv0:dsh.kv1]),
+                dev(kcf[seqs][:, :, dsh.kv0:dsh.kv1]), dev(vcf[seqs][:, :, dsh.kv0:dsh.kv1]))
+        sidx = torch.tensor(seqs, dtype=torch.int32, device="cuda")
+        same = True
+        for _ in range(3):
+            eb.attention_decode_batched_gather(ddesc, layer, len(seqs),
+                                               torch.from_numpy(np.ascontiguousarray(lpos)).cuda(),
+                                               mp, *args, max_seq * dsh.n_kv_heads * hd, g.next(),
+                                               sidx, wsg)
+            g.finish()
+            if head_groups is None:
+                same &= torch.equal(g.full, fulld)
+        torch.cuda.synchronize()
+        if head_groups is None:
+            print(f"[mgpu] rank {rank} decode gathered in-kernel == NCCL gather: {same}",
+                  flush=True)
+            ok &= same
+        elif rank == 0:
+            got = g.full.float().cpu().numpy().ravel()
+            ma, rl = orc.max_abs(got, want), orc.rel_l2(got, want)
+            print(f"[mgpu] world={world} decode split by sequence (gathered in-kernel): "
+                  f"max_abs={ma:.2e} rel_l2={rl:.2e}", flush=True)
+            ok &= ma <= 2e-3 and rl <= 1e-3
+        del g
     flag = torch.tensor([0 if ok else 1], device="cuda")
     dist.all_reduce(flag)
     dist.barrier()
