@@ -6,13 +6,15 @@
 //
 // One CTA = NQ query tiles of 128 rows (the two heads of a GQA pair when the
 // group size is even, so each K/V tile feeds twice the MMA work):
-//   warp 0      TMA producer: the query tiles (already normalised, rotated and
-//               rounded to the operand type by the row-prep pass), then K and
-//               V tiles [BN rows x 64 dims] (128-byte swizzle) into separate
-//               NSTK- and NSTV-deep shared-memory rings.
+//   warp 0      TMA producer: the query tiles (normalised, rotated and
+//               rounded by the row-prep pass, or the raw 16-bit rows the
+//               softmax warps transform in place), then K tiles [BN rows x 64
+//               dims] (128-byte swizzle) into an NSTK-deep ring.
 //   warp 1      TMEM owner + MMA issuer (one thread): S_t = Q_t K^T into TMEM,
 //               then O_t += P_t V with P read from TMEM (it overwrites S_t).
-//   warps 2-3   idle (softmax warps must start at a multiple of 4: a warp may
+//   warp 2      TMA producer of the V ring (its own thread, so K loads never
+//               queue behind a V slot).
+//   warp 3      idle (softmax warps must start at a multiple of 4: a warp may
 //               only address TMEM lanes 32*(warp%4)..+31).
 //   warps 4..   one thread per query row of each tile: per KV tile read the S
 //               row from TMEM, online softmax in f32 (exp2 on MUFU, some
@@ -23,10 +25,13 @@
 // reference attends the same post-RoPE k / post-norm v it writes,
 // crates/eyebrowse-nn/src/attention.rs:78-115).
 //
-// f32 caches (SPLIT): every operand x is carried as two f16 values
-// hi = f16(x), lo = f16(x - hi); S = Qh.Kh + Qh.Kl + Ql.Kh and
-// O += Ph.Vh + Ph.Vl + Pl.Vh (the standard error-compensated split, which
-// keeps ~21 mantissa bits on f16 tensor cores).
+// f32 caches (SPLIT): every q/k/v operand x is carried as two f16 values
+// hi = f16(x), lo = f16(x - hi), and S = Qh.Kh + Qh.Kl + Ql.Kh (the standard
+// error-compensated split, ~21 mantissa bits on f16 tensor cores: the
+// logits need them, an f16 rounding of q or k moves a logit of a
+// unit-RMS head_dim-256 row by ~1e-2). P lies in [0, 1] and is kept at f16
+// only, O += Ph.Vh + Ph.Vl: its rounding perturbs each weight by at most
+// 2^-12 relative, an output error below 1.5e-4 * max|v|.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -70,7 +75,8 @@ struct PfCfg {
   static constexpr int THREADS = 128 + 128 * NQ;
   // Of every 8 column pairs of P, this many take their exp2 on the FMA pipe
   // (ex2_fma_pair) and the rest on MUFU. The hi/lo split path keeps MUFU for
-  // all: its P carries ~21 bits, beyond the polynomial's accuracy.
+  // all: its tiles are bound by the MMA issue of three QK passes, not by
+  // the exponentials.
   static constexpr int EMU_PAIRS = SPLIT ? 0 : kEmuPairsOf8;
   static_assert(HD % 64 == 0 && HD <= 256, "head_dim");
   static_assert(BN % 32 == 0 && BN <= 128, "kv tile");
@@ -274,62 +280,56 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    // K tile j uses K slot j % NSTK and is released when its QK MMAs
-    // complete; V tile j uses V slot j % NSTV, released after its PV MMAs.
-    // K gets the deeper ring: K_{j+1} is needed one step after K_{j+1-NSTK}
-    // frees, V_{j+1} two steps after V_{j+1-NSTV}.
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------ TMA producers
+    // Warp 0 loads the query tiles and the K ring, warp 2 the V ring, each
+    // from its own thread: K tile j uses K slot j % NSTK and is released when
+    // its QK MMAs complete; V tile j uses V slot j % NSTV, released after its
+    // PV MMAs. Separate threads let K_{j+NSTK} load as soon as QK_j is done,
+    // without waiting behind V_{j+1}'s slot (with one-deep rings that wait
+    // would put a load latency on every tile).
     if (lane == 0) {
-      // The query tiles (rows past S read as zeros): NQ heads x HB boxes of
-      // [128 rows x 64 dims], hi and lo planes when split.
-      mbar_arrive_expect_tx(bar(kBarQ), C::Q_BYTES);
+      const bool is_k = warp == 0;
+      if (is_k) {
+        // The query tiles (rows past S read as zeros): NQ heads x HB boxes of
+        // [128 rows x 64 dims], hi and lo planes when split.
+        mbar_arrive_expect_tx(bar(kBarQ), C::Q_BYTES);
 #pragma unroll
-      for (int t = 0; t < NQ; t++)
+        for (int t = 0; t < NQ; t++)
 #pragma unroll
-        for (int hb = 0; hb < C::HB; hb++) {
-          const uint32_t dst = sQ + t * C::QT_BYTES + hb * C::TILE128;
-          tma_load_3d(dst, &tmQ, bar(kBarQ), hb * 64, grp * NQ + t, q0);
-          if (SPLIT) tma_load_3d(dst + C::HB * C::TILE128, &tmQlo, bar(kBarQ), hb * 64, grp * NQ + t, q0);
-        }
-      int kiss[NSTK], viss[NSTV];
-      for (int s = 0; s < NSTK; s++) kiss[s] = 0;
-      for (int s = 0; s < NSTV; s++) viss[s] = 0;
+          for (int hb = 0; hb < C::HB; hb++) {
+            const uint32_t dst = sQ + t * C::QT_BYTES + hb * C::TILE128;
+            tma_load_3d(dst, &tmQ, bar(kBarQ), hb * 64, grp * NQ + t, q0);
+            if (SPLIT)
+              tma_load_3d(dst + C::HB * C::TILE128, &tmQlo, bar(kBarQ), hb * 64, grp * NQ + t, q0);
+          }
+      }
+      const int NST = is_k ? NSTK : NSTV;
+      const uint32_t ring = is_k ? sK : sV;
+      const int full0 = is_k ? kKFull0 : kVFull0, empty0 = is_k ? kKEmpty0 : kVEmpty0;
+      const CUtensorMap* hi = is_k ? &tmK : &tmV;
+      const CUtensorMap* lo = is_k ? &tmKlo : &tmVlo;
+      const uint32_t err_bit = kErrTimeoutTma;
+      int iss[NSTK > NSTV ? NSTK : NSTV];
+      for (int s = 0; s < NST; s++) iss[s] = 0;
       for (int j = 0; j < n_tiles; j++) {
-        const int sk = j % NSTK, sv = j % NSTV;
-        const uint32_t kst = sK + sk * C::K_BYTES;
-        const uint32_t vst = sV + sv * C::K_BYTES;
-        if (j >= NSTK && !mbar_wait(bar(kKEmpty0 + sk), (j / NSTK - 1) & 1, abort_flag, a.err,
-                                    kErrTimeoutTma))
+        const int sl = j % NST;
+        const uint32_t dst = ring + sl * C::K_BYTES;
+        if (j >= NST && !mbar_wait(bar(empty0 + sl), (j / NST - 1) & 1, abort_flag, a.err, err_bit))
           break;
-        const uint32_t kf = bar(kKFull0 + sk);
-        mbar_arrive_expect_tx(kf, C::K_BYTES);
+        const uint32_t fb = bar(full0 + sl);
+        mbar_arrive_expect_tx(fb, C::K_BYTES);
 #pragma unroll
         for (int hb = 0; hb < C::HB; hb++) {
-          tma_load_3d(kst + hb * C::KV_BOX, &tmK, kf, hb * 64, kvh, (j0 + j) * BN);
-          if (SPLIT)
-            tma_load_3d(kst + (C::HB + hb) * C::KV_BOX, &tmKlo, kf, hb * 64, kvh, (j0 + j) * BN);
+          tma_load_3d(dst + hb * C::KV_BOX, hi, fb, hb * 64, kvh, (j0 + j) * BN);
+          if (SPLIT) tma_load_3d(dst + (C::HB + hb) * C::KV_BOX, lo, fb, hb * 64, kvh, (j0 + j) * BN);
         }
-        kiss[sk]++;
-        if (j >= NSTV && !mbar_wait(bar(kVEmpty0 + sv), (j / NSTV - 1) & 1, abort_flag, a.err,
-                                    kErrTimeoutTma))
-          break;
-        const uint32_t vf = bar(kVFull0 + sv);
-        mbar_arrive_expect_tx(vf, C::K_BYTES);
-#pragma unroll
-        for (int hb = 0; hb < C::HB; hb++) {
-          tma_load_3d(vst + hb * C::KV_BOX, &tmV, vf, hb * 64, kvh, (j0 + j) * BN);
-          if (SPLIT)
-            tma_load_3d(vst + (C::HB + hb) * C::KV_BOX, &tmVlo, vf, hb * 64, kvh, (j0 + j) * BN);
-        }
-        viss[sv]++;
+        iss[sl]++;
       }
       // Every issued copy has landed before the CTA can exit.
-      mbar_drain(bar(kBarQ), 0, a.err, kErrTimeoutTma);
-      for (int s = 0; s < NSTK; s++)
-        if (kiss[s]) mbar_drain(bar(kKFull0 + s), (kiss[s] - 1) & 1, a.err, kErrTimeoutTma);
-      for (int s = 0; s < NSTV; s++)
-        if (viss[s]) mbar_drain(bar(kVFull0 + s), (viss[s] - 1) & 1, a.err, kErrTimeoutTma);
+      if (is_k) mbar_drain(bar(kBarQ), 0, a.err, err_bit);
+      for (int s = 0; s < NST; s++)
+        if (iss[s]) mbar_drain(bar(full0 + s), (iss[s] - 1) & 1, a.err, err_bit);
     }
     __syncwarp();  // reconverge before the CTA barrier below
   } else if (warp == 1) {
@@ -363,11 +363,9 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         const uint32_t vst = sV + sv * C::K_BYTES;
         const uint32_t tP = tmem + C::S_COL0 + (t * NSB + b) * BN;
         const uint32_t tO = tmem + t * HD;
-        constexpr int NPASS = SPLIT ? 3 : 1;
+        constexpr int NPASS = SPLIT ? 2 : 1;
 #pragma unroll
-        for (int pass = 0; pass < NPASS; pass++) {
-          const int pa = (pass == 2) ? 1 : 0;  // Ph Vh, Ph Vl, Pl Vh
-          const int vb = (pass == 1) ? 1 : 0;
+        for (int vb = 0; vb < NPASS; vb++) {  // P Vh, then P Vl
 #pragma unroll
           for (int kk = kk0; kk < kk1; kk++) {
             const uint64_t bd =
@@ -375,9 +373,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
             // column of P elements [16kk, 16kk+16) in the softmax's layout
             constexpr int HALF = BN >= 64 ? 64 : BN;
             const int blk = (kk * 16) / HALF, within = (kk * 16) % HALF;
-            const uint32_t col = SPLIT ? blk * HALF + within / 2 + pa * (HALF / 2)
-                                       : blk * (HALF / 2) + within / 2;
-            umma_ts(tO, tP + col, bd, idesc_pv, (!first || pass > 0 || kk > 0) ? 1u : 0u);
+            const uint32_t col = blk * (HALF / 2) + within / 2;
+            umma_ts(tO, tP + col, bd, idesc_pv, (!first || vb > 0 || kk > 0) ? 1u : 0u);
           }
         }
       };
@@ -598,7 +595,6 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
           }
         }
         uint32_t ph[HALF / 2];
-        uint32_t pl[SPLIT ? HALF / 2 : 1];
 #pragma unroll
         for (int c = 0; c < HALF; c += 2) {
           float y0, y1, p0, p1;
@@ -610,26 +606,13 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
             p1 = ex2(y1);
           }
           rsum2[(c >> 1) & 3] = f2_add(rsum2[(c >> 1) & 3], f2_pack(p0, p1));
-          if (SPLIT) {
-            const __half2 hh = __floats2half2_rn(p0, p1);
-            const float2 hf = __half22float2(hh);
-            ph[c / 2] = *reinterpret_cast<const uint32_t*>(&hh);
-            pl[c / 2] = pack_half2(p0 - hf.x, p1 - hf.y);
-          } else {
-            ph[c / 2] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
-          }
+          ph[c / 2] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
         }
-        // P layout (32-bit TMEM columns, two 16-bit values each): half h of a
-        // plain P takes columns [h*HALF/2, (h+1)*HALF/2); with hi/lo planes
-        // half h takes [h*HALF, (h+1)*HALF), hi first then lo. Either way it
-        // only covers S columns this pass has already read.
+        // P layout (32-bit TMEM columns, two 16-bit values each): half h
+        // takes columns [h*HALF/2, (h+1)*HALF/2), S columns this pass has
+        // already read.
         if constexpr (HALF == 64) {
-          if (SPLIT) {
-            tmem_st32(tS + hbase, ph);
-            tmem_st32(tS + hbase + 32, *reinterpret_cast<uint32_t(*)[32]>(pl));
-          } else {
-            tmem_st32(tS + hbase / 2, ph);
-          }
+          tmem_st32(tS + hbase / 2, ph);
         } else {  // BN == 32: one 16-column store per plane
           asm volatile(
               "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -638,14 +621,6 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
               "r"(ph[7]), "r"(ph[8]), "r"(ph[9]), "r"(ph[10]), "r"(ph[11]), "r"(ph[12]),
               "r"(ph[13]), "r"(ph[14]), "r"(ph[15])
               : "memory");
-          if (SPLIT)
-            asm volatile(
-                "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-                "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tS + BN / 2),
-                "r"(pl[0]), "r"(pl[1]), "r"(pl[2]), "r"(pl[3]), "r"(pl[4]), "r"(pl[5]),
-                "r"(pl[6]), "r"(pl[7]), "r"(pl[8]), "r"(pl[9]), "r"(pl[10]), "r"(pl[11]),
-                "r"(pl[12]), "r"(pl[13]), "r"(pl[14]), "r"(pl[15])
-                : "memory");
         }
         if constexpr (BN == 128) {
           if (hbase == 0) {
@@ -930,7 +905,7 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* q16, con
       case 64:
         return run_prefill<64, 128, 1, true, false, 2, 2>(a, q16, k16, v16, split, g, st);
       case 128: return run_prefill<128, 64, 1, true, false, 2, 2>(a, q16, k16, v16, split, g, st);
-      case 256: return run_prefill<256, 32, 1, true, false, 1, 1>(a, q16, k16, v16, split, g, st);
+      case 256: return run_prefill<256, 32, 1, true, false, 2, 1>(a, q16, k16, v16, split, g, st);
     }
   } else if (bf16) {
     switch (hd) {
