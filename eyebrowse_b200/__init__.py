@@ -360,6 +360,10 @@ def device_error() -> int:
     return bits.value
 
 
+DEVICE_ERROR_TMA = 1 << 0       # bits of the device error word (EB_DEVICE_ERROR_*)
+DEVICE_ERROR_MMA = 1 << 1
+DEVICE_ERROR_SOFTMAX = 1 << 2
+DEVICE_ERROR_EPILOGUE = 1 << 3
 DEVICE_ERROR_SELFTEST = 1 << 5
 
 

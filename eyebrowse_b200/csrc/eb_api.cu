@@ -11,6 +11,12 @@
 #include "eb_common.cuh"
 #include "eb_kernels.cuh"
 
+static_assert(eb::kErrTimeoutTma == EB_DEVICE_ERROR_TMA && eb::kErrTimeoutMma == EB_DEVICE_ERROR_MMA &&
+                  eb::kErrTimeoutSoftmax == EB_DEVICE_ERROR_SOFTMAX &&
+                  eb::kErrTimeoutEpilogue == EB_DEVICE_ERROR_EPILOGUE &&
+                  eb::kErrTimeoutSelftest == EB_DEVICE_ERROR_SELFTEST,
+              "device error bits");
+
 namespace eb {
 
 // Device error word: bounded waits that give up set bits here.

@@ -15,15 +15,17 @@ namespace eb {
 
 enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
 
-// Device error word bits (set by bounded waits that gave up; read by eb_get_device_error).
+// Device error word bits (set by bounded waits that gave up; read by
+// eb_get_device_error). The header's EB_DEVICE_ERROR_* (checked in
+// eb_api.cu).
 enum : unsigned {
   kErrTimeoutTma = 1u << 0,
   kErrTimeoutMma = 1u << 1,
   kErrTimeoutSoftmax = 1u << 2,
   kErrTimeoutEpilogue = 1u << 3,
-  kErrTimeoutProducer = 1u << 4,
   kErrTimeoutSelftest = 1u << 5,  // eb_selftest_wait_timeout's wait (no real kernel failed)
 };
+
 
 // A bounded wait gives up after this long (device globaltimer, ns). Normal
 // waits are microseconds; a second only elapses when a partner never arrives.

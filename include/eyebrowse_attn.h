@@ -326,6 +326,11 @@ EB_API int eb_head_broadcast(const void* local, void* multicast, int64_t rows,
  * eb_attention_decode_noalloc. (A caller workspace shared by the failed call
  * needs eb_workspace_init again.) */
 EB_API int eb_get_device_error(uint32_t* bits);
+/* Bits of the device error word: the role whose bounded wait gave up. */
+#define EB_DEVICE_ERROR_TMA (1u << 0)      /* a TMA producer (load ring slot or drain) */
+#define EB_DEVICE_ERROR_MMA (1u << 1)      /* an MMA issuer (operands, P, its own commits) */
+#define EB_DEVICE_ERROR_SOFTMAX (1u << 2)  /* a softmax / online-softmax thread */
+#define EB_DEVICE_ERROR_EPILOGUE (1u << 3) /* an epilogue (final accumulator, output stores) */
 
 /* Checks the failure path of the kernels' bounded waits on this device: a
  * one-CTA kernel waits on a barrier that nothing completes, gives up after

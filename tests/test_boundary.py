@@ -33,6 +33,15 @@ def test_library_exports_every_declared_symbol(eb):
     assert set(eb.EXPORTS) == _declared()
 
 
+def test_device_error_bits_match_the_header(eb):
+    txt = open(os.path.join(ROOT, "include", "eyebrowse_attn.h")).read()
+    bits = {m[0]: int(m[1]) for m in re.findall(r"#define EB_DEVICE_ERROR_(\w+) \(1u << (\d+)\)", txt)}
+    assert set(bits) == {"TMA", "MMA", "SOFTMAX", "EPILOGUE", "SELFTEST"}
+    for name, shift in bits.items():
+        assert getattr(eb, f"DEVICE_ERROR_{name}") == 1 << shift, name
+    assert len(set(bits.values())) == len(bits)
+
+
 def test_rope_tables_match_oracle_bitwise(eb, orc):
     for (ms, hd, th, ra) in [(64, 128, 1e6, None), (40, 256, 1e6, 32), (8, 4, 1e4, None),
                              (33, 64, 5e5, 3)]:
