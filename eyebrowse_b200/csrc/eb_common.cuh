@@ -335,6 +335,17 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   return d;
 }
 
+// The same descriptor for an operand `bytes` further on (a multiple of 16):
+// the start-address field is the descriptor's lowest field, and shared
+// memory addresses stay below 256 KB (the field's 14 bits), so a plain add
+// never carries out of it. An issuing thread builds one descriptor per
+// buffer and adds compile-time offsets: at one MMA per k-step of 16 the
+// per-MMA field arithmetic of sdesc_sw128 is a measurable part of the issue
+// time.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t desc, uint32_t bytes) {
+  return desc + (uint64_t)(bytes >> 4);
+}
+
 // Instruction descriptor for tcgen05.mma kind::f16 with f32 accumulation.
 //   [4,6) D format 1=F32; [7,10) A fmt, [10,13) B fmt (0=F16, 1=BF16);
 //   [15] A major (0=K), [16] B major (0=K, 1=MN); [17,23) N>>3; [24,29) M>>4.

@@ -29,9 +29,12 @@
 // hi = f16(x), lo = f16(x - hi), and S = Qh.Kh + Qh.Kl + Ql.Kh (the standard
 // error-compensated split, ~21 mantissa bits on f16 tensor cores: the
 // logits need them, an f16 rounding of q or k moves a logit of a
-// unit-RMS head_dim-256 row by ~1e-2). P lies in [0, 1] and is kept at f16
-// only, O += Ph.Vh + Ph.Vl: its rounding perturbs each weight by at most
-// 2^-12 relative, an output error below 1.5e-4 * max|v|.
+// unit-RMS head_dim-256 row by ~1e-2). P (at most 2^8 under the lazy
+// rescale) is kept at f16 only, O += P.Vh + P.Vl, and l sums those same f16
+// values: o is then an exact convex combination of v rows whose weights are
+// each off by at most 2^-11 relative and still sum to one, so the error is
+// at most 2^-11 times the weighted spread of v about o (none when one key
+// carries all the weight).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -58,9 +61,16 @@ constexpr int kEmuPairsOf8 = EB_PREFILL_EMU_PAIRS;
 template <int HD, int BN, int NQ, bool SPLIT, int NSTK, int NSTV>
 struct PfCfg {
   static constexpr int NQP = SPLIT ? 2 : 1;  // operand planes (hi, lo)
+  // Split operands at head_dim 256: Q's hi plane lives in tensor memory (the
+  // A operand of the Qh.Kh and Qh.Kl MMAs) and only its lo plane in shared
+  // memory. The 64 KB this frees makes room for 64-key K/V tiles, so each
+  // QK MMA covers twice the keys (the MMA thread's issue rate bounds this
+  // kernel).
+  static constexpr bool QT = SPLIT && HD == 256;
+  static constexpr int NQP_SMEM = QT ? 1 : NQP;  // Q planes in shared memory
   static constexpr int HB = HD / 64;         // 64-element boxes along head_dim
   static constexpr int TILE128 = 128 * 128;  // one [128 rows x 128 B] box
-  static constexpr int QT_BYTES = NQP * HB * TILE128;
+  static constexpr int QT_BYTES = NQP_SMEM * HB * TILE128;
   static constexpr int Q_BYTES = NQ * QT_BYTES;
   static constexpr int KV_BOX = BN * 128;  // one [BN rows x 128 B] box
   static constexpr int K_BYTES = NQP * HB * KV_BOX;  // one K (or V) tile, all planes
@@ -68,9 +78,11 @@ struct PfCfg {
   static constexpr int BAR_OFF = V_OFF + NSTV * K_BYTES;
   static constexpr int SMEM = BAR_OFF + 512 + 1024;  // barriers/flags + alignment slack
   static constexpr int NSB = (NQ == 1 || NQ * HD + NQ * 2 * BN <= 512) ? 2 : 1;
-  // TMEM columns: the O accumulators first ([t*HD, (t+1)*HD)), then the S/P
-  // buffers; every MMA destination starts at a column aligned to its width.
-  static constexpr int S_COL0 = NQ * HD;
+  // TMEM columns: the O accumulators first ([t*HD, (t+1)*HD)), then Q's hi
+  // plane when QT (HD/2 columns of packed f16 pairs), then the S/P buffers;
+  // every MMA destination starts at a column aligned to its width.
+  static constexpr int Q_TM = NQ * HD;
+  static constexpr int S_COL0 = NQ * HD + (QT ? HD / 2 : 0);
   static constexpr int TMEM_COLS = constexpr_pow2ceil(S_COL0 + NQ * NSB * BN);
   static constexpr int THREADS = 128 + 128 * NQ;
   // Of every 8 column pairs of P, this many take their exp2 on the FMA pipe
@@ -81,6 +93,7 @@ struct PfCfg {
   static_assert(HD % 64 == 0 && HD <= 256, "head_dim");
   static_assert(BN % 32 == 0 && BN <= 128, "kv tile");
   static_assert(TMEM_COLS <= 512, "tensor memory budget");
+  static_assert(!QT || NQ == 1, "Q in tensor memory: one query tile");
   static_assert(SMEM <= 232448, "shared memory budget");
   // Head-gather epilogue: tile t's O stages at [t*STG, (t+1)*STG) from the
   // start of shared memory (q and the K/V rings are idle by then), as
@@ -111,6 +124,43 @@ struct GatherMaps {
 // as they are. Then the
 // generic-proxy writes are made visible to the tensor core and the tile's
 // ready barrier (128 arrivals) is arrived on.
+// Q in tensor memory (f32 caches at head_dim 256): thread r of the softmax
+// warpgroup copies its query row's f16 hi plane (HD values, already
+// normalised, rotated and split by the row-prep pass) into its TMEM lane,
+// element k at column k/2 of the given base, low half first -- the layout
+// of an A operand read from tensor memory (the same as P's). Rows past S
+// store zeros. The stores are warp-collective, so every thread makes them.
+// Then the tile's ready barrier (128 arrivals) tells the MMA thread.
+template <int HD>
+__device__ __forceinline__ void q_hi_to_tmem(const PrefillArgs& a, uint32_t taddr, int q_row,
+                                             int h, bool valid, uint32_t ready_bar) {
+  const uint4* src =
+      reinterpret_cast<const uint4*>(a.q_hi + ((int64_t)(valid ? q_row : 0) * a.H + h) * HD);
+#pragma unroll
+  for (int half = 0; half < HD / 128; half++) {
+    // 128 values = 16 loads in flight, then two 32-column stores
+    uint4 x[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+      x[i] = valid ? __ldg(src + half * 16 + i) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+      uint32_t w[32];
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        w[4 * i] = x[c * 8 + i].x;
+        w[4 * i + 1] = x[c * 8 + i].y;
+        w[4 * i + 2] = x[c * 8 + i].z;
+        w[4 * i + 3] = x[c * 8 + i].w;
+      }
+      tmem_st32(taddr + half * 64 + c * 32, w);
+    }
+  }
+  tmem_st_wait();
+  tc_fence_before();
+  mbar_arrive(ready_bar);
+}
+
 template <int HD, bool BF16>
 __device__ __forceinline__ void q_tile_transform(uint32_t tile, int r, int q_row,
                                                  const PrefillArgs& a, uint32_t q_bar,
@@ -299,9 +349,14 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
 #pragma unroll
           for (int hb = 0; hb < C::HB; hb++) {
             const uint32_t dst = sQ + t * C::QT_BYTES + hb * C::TILE128;
-            tma_load_3d(dst, &tmQ, bar(kBarQ), hb * 64, grp * NQ + t, q0);
-            if (SPLIT)
-              tma_load_3d(dst + C::HB * C::TILE128, &tmQlo, bar(kBarQ), hb * 64, grp * NQ + t, q0);
+            if constexpr (C::QT) {  // lo plane only: the hi plane goes to TMEM
+              tma_load_3d(dst, &tmQlo, bar(kBarQ), hb * 64, grp * NQ + t, q0);
+            } else {
+              tma_load_3d(dst, &tmQ, bar(kBarQ), hb * 64, grp * NQ + t, q0);
+              if (SPLIT)
+                tma_load_3d(dst + C::HB * C::TILE128, &tmQlo, bar(kBarQ), hb * 64, grp * NQ + t,
+                            q0);
+            }
           }
       }
       const int NST = is_k ? NSTK : NSTV;
@@ -337,10 +392,14 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(128, BN, BF16, false);
       constexpr uint32_t idesc_pv = idesc_f16(128, HD, BF16, true);
+      // Base descriptors of the query tiles, the K ring and the V ring; each
+      // MMA's operand is a constant offset from one of them (sdesc_add).
+      const uint64_t dQ0 = sdesc_sw128(sQ, 16, 1024);
+      const uint64_t dK0 = sdesc_sw128(sK, 16, 1024);
+      const uint64_t dV0 = sdesc_sw128(sV, C::KV_BOX, 1024);
       // S_t(buffer b) = Q_t K^T
       auto issue_qk = [&](int t, int b, int sk) {
-        const uint32_t kst = sK + sk * C::K_BYTES;
-        const uint32_t qb = sQ + t * C::QT_BYTES;
+        const uint64_t dK = sdesc_add(dK0, sk * C::K_BYTES);
         const uint32_t tS = tmem + C::S_COL0 + (t * NSB + b) * BN;
         constexpr int NPASS = SPLIT ? 3 : 1;
 #pragma unroll
@@ -350,17 +409,24 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
 #pragma unroll
           for (int kk = 0; kk < HD / 16; kk++) {
             const int hb = kk >> 2, w = kk & 3;
-            const uint64_t ad = sdesc_sw128(qb + (qa * C::HB + hb) * C::TILE128 + w * 32, 16, 1024);
-            const uint64_t bd =
-                sdesc_sw128(kst + (kb * C::HB + hb) * C::KV_BOX + w * 32, 16, 1024);
-            umma_ss(tS, ad, bd, idesc_qk, (pass > 0 || kk > 0) ? 1u : 0u);
+            const uint64_t bd = sdesc_add(dK, (kb * C::HB + hb) * C::KV_BOX + w * 32);
+            const uint32_t acc = (pass > 0 || kk > 0) ? 1u : 0u;
+            if (C::QT && qa == 0) {
+              // Qh from tensor memory: k-step kk is columns [8kk, 8kk+8)
+              umma_ts(tS, tmem + C::Q_TM + kk * 8, bd, idesc_qk, acc);
+            } else {
+              const int plane = C::QT ? 0 : qa;  // QT keeps only Ql in shared memory
+              const uint64_t ad =
+                  sdesc_add(dQ0, t * C::QT_BYTES + (plane * C::HB + hb) * C::TILE128 + w * 32);
+              umma_ss(tS, ad, bd, idesc_qk, acc);
+            }
           }
         }
       };
       // O_t += P_t V, P_t read from tensor memory (the S buffer it replaced)
       // keys [16*kk0, 16*kk1) of the tile
       auto issue_pv = [&](int t, int b, int sv, bool first, int kk0, int kk1) {
-        const uint32_t vst = sV + sv * C::K_BYTES;
+        const uint64_t dV = sdesc_add(dV0, sv * C::K_BYTES);
         const uint32_t tP = tmem + C::S_COL0 + (t * NSB + b) * BN;
         const uint32_t tO = tmem + t * HD;
         constexpr int NPASS = SPLIT ? 2 : 1;
@@ -368,8 +434,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         for (int vb = 0; vb < NPASS; vb++) {  // P Vh, then P Vl
 #pragma unroll
           for (int kk = kk0; kk < kk1; kk++) {
-            const uint64_t bd =
-                sdesc_sw128(vst + vb * C::HB * C::KV_BOX + kk * 16 * 128, C::KV_BOX, 1024);
+            const uint64_t bd = sdesc_add(dV, vb * C::HB * C::KV_BOX + kk * 16 * 128);
             // column of P elements [16kk, 16kk+16) in the softmax's layout
             constexpr int HALF = BN >= 64 ? 64 : BN;
             const int blk = (kk * 16) / HALF, within = (kk * 16) % HALF;
@@ -384,7 +449,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
       if (ok && mbar_wait(bar(kKFull0), 0, abort_flag, a.err, kErrTimeoutMma)) {
 #pragma unroll
         for (int t = 0; t < NQ; t++) {
-          if (a.q_fused && !mbar_wait(bar(kQReady0 + t), 0, abort_flag, a.err, kErrTimeoutMma)) {
+          if ((a.q_fused || C::QT) &&
+              !mbar_wait(bar(kQReady0 + t), 0, abort_flag, a.err, kErrTimeoutMma)) {
             ok = false;
             break;
           }
@@ -480,6 +546,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     const uint32_t tO = tmem + lane_off + t * HD;
     if (a.q_fused) q_tile_transform<HD, BF16>(sQ + t * C::QT_BYTES, r, q_row, a, bar(kBarQ),
                                              bar(kQReady0 + t), abort_flag);
+    if constexpr (C::QT) q_hi_to_tmem<HD>(a, tmem + lane_off + C::Q_TM, q_row, h, valid,
+                                          bar(kQReady0 + t));
     // With a window the running max starts finite: a row can see no key of
     // its first tiles (S row all -inf), and -inf - (-inf) would turn its P
     // into NaN. Any finite score later rescales by ex2(-1e30 - m) = 0.
@@ -605,8 +673,16 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
             p0 = ex2(y0);
             p1 = ex2(y1);
           }
-          rsum2[(c >> 1) & 3] = f2_add(rsum2[(c >> 1) & 3], f2_pack(p0, p1));
           ph[c / 2] = BF16 ? pack_bf162(p0, p1) : pack_half2(p0, p1);
+          if constexpr (SPLIT) {
+            // l sums the f16 values the PV MMAs use, so the weights p/l sum
+            // to one exactly and P's rounding largely cancels (at scale 1.0
+            // one key can carry nearly all the weight: o ~ v(1 + delta)).
+            const float2 pr = __half22float2(*reinterpret_cast<const __half2*>(&ph[c / 2]));
+            p0 = pr.x;
+            p1 = pr.y;
+          }
+          rsum2[(c >> 1) & 3] = f2_add(rsum2[(c >> 1) & 3], f2_pack(p0, p1));
         }
         // P layout (32-bit TMEM columns, two 16-bit values each): half h
         // takes columns [h*HALF/2, (h+1)*HALF/2), S columns this pass has
@@ -819,8 +895,10 @@ static cudaError_t run_prefill_k(const PrefillArgs& a, const void* q16, const vo
     __atomic_fetch_or(&configured, 1u << (dev & 31), __ATOMIC_RELEASE);
   }
   CUtensorMap mq, mql, mk, mv, mkl, mvl;
+  const __half* ka_q_hi = nullptr;
   if (SPLIT) {
     const __half* qp = reinterpret_cast<const __half*>(q16);
+    ka_q_hi = qp;
     if (!make_kv_map(&mq, qp, a.S, a.H, HD, 128, false) ||
         !make_kv_map(&mql, qp + (size_t)a.S * a.H * HD, a.S, a.H, HD, 128, false))
       return cudaErrorInvalidValue;
@@ -850,6 +928,7 @@ static cudaError_t run_prefill_k(const PrefillArgs& a, const void* q16, const vo
   memset(&gm, 0, sizeof(gm));
   PrefillArgs ka = a;
   ka.n_dst = 0;
+  ka.q_hi = ka_q_hi;
   if (g && g->n_dst > 0) {
     if (g->n_dst > kMaxGather) return cudaErrorInvalidValue;
     for (int d = 0; d < g->n_dst; d++)
@@ -905,7 +984,7 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, int hd, const void* q16, con
       case 64:
         return run_prefill<64, 128, 1, true, false, 2, 2>(a, q16, k16, v16, split, g, st);
       case 128: return run_prefill<128, 64, 1, true, false, 2, 2>(a, q16, k16, v16, split, g, st);
-      case 256: return run_prefill<256, 32, 1, true, false, 2, 1>(a, q16, k16, v16, split, g, st);
+      case 256: return run_prefill<256, 64, 1, true, false, 1, 1>(a, q16, k16, v16, split, g, st);
     }
   } else if (bf16) {
     switch (hd) {
