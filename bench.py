@@ -62,7 +62,7 @@ KERNEL_SOURCES = {
     "prefill_cfg4": ("eb_prefill.cu", "eb_common.cuh", "eb_tc.cuh"),
     "prep_cfg3": ("eb_small.cu", "eb_rowops.cuh", "eb_common.cuh"),
     "decode_cfg5": ("eb_decode_tc.cu", "eb_common.cuh", "eb_tc.cuh"),
-    "decode_cfg2": ("eb_decode.cu", "eb_common.cuh", "eb_rowops.cuh"),
+    "decode_cfg2": ("eb_decode_cl.cu", "eb_decode_out.cuh", "eb_common.cuh", "eb_rowops.cuh"),
     "linear_proj3": ("eb_linear.cu", "eb_common.cuh", "eb_tc.cuh"),
 }
 
