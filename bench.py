@@ -80,6 +80,14 @@ def source_hash(key: str):
     return h.hexdigest()[:16]
 
 
+def rank_traffic(key: str, share: float):
+    """profile_traffic scaled to one rank's launch: the captures are of the
+    one-GPU workload, and a rank of a sharded run processes `share` of its
+    units (heads, or sequences x heads) in a launch of the same kernel."""
+    t = profile_traffic(key)
+    return None if t is None else t * share
+
+
 def profile_traffic(key: str):
     """Per-launch DRAM traffic recorded from an ncu capture in profiles/*.md
     (a line `traffic[<key>]: <bytes per launch> ... source <hash>`), or None
@@ -1070,6 +1078,7 @@ def main():
         peak_unit, peak_name = "TFLOP/s", "bf16_tflops_sustained"
     else:
         total_units = w.bytes_total()
+        kern_units = w.kernel_units()
         unit, bound = "GB/s", "hbm"
         value = total_units / (res["ms_per_step"] * 1e-3) / 1e9
         achieved = w.kernel_units() / (res["kernel_ms"] * 1e-3) / 1e9
@@ -1113,7 +1122,8 @@ def main():
                   "ms_per_step": dres["ms_per_step"], "config": dw.describe(world),
                   "roofline": {"bound": "hbm", "achieved": dach, "peak": peaks.get("hbm_gbs"),
                                "unit": "GB/s", "frac": dach / peaks.get("hbm_gbs"),
-                               "traffic": profile_traffic("decode_cfg5"),
+                               "traffic": rank_traffic("decode_cfg5", dw.kernel_units() /
+                                                       dw.bytes_total() if world > 1 else 1.0),
                                "peak_source": f"{peak_kind} hbm_gbs"}}
         if not args.no_cpu and rank == 0 and world == 1:
             decode["cpu_baseline"] = cpu_baseline_decode(dw)
@@ -1145,7 +1155,9 @@ def main():
                            untimed_warm_s=WARM_S),
             "cuda_graph_steps": res.get("graph_reps", 0),
             "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": peak_unit,
-                         "frac": achieved / peak, "traffic": profile_traffic(tkey) if tkey else None,
+                         "frac": achieved / peak,
+                         "traffic": (rank_traffic(tkey, kern_units / total_units if world > 1 else 1.0)
+                                     if tkey else None),
                          "peak_source": f"{peak_kind} {peak_name}",
                          "kernel_ms": res["kernel_ms"]},
             "cpu_baseline": cpu,
