@@ -386,10 +386,13 @@ static size_t kv_split_bytes(int64_t s, int64_t hkv, int64_t hd) {
 static size_t q_prep_bytes(int64_t s, int64_t h, int64_t hd, bool split) {
   return round_up((size_t)(split ? 2 : 1) * s * h * hd * sizeof(__half));
 }
+// f32 K/V at head_dim 256: the attention kernel reads the raw q rows and
+// normalises, rotates and splits them itself (no q pass, no q planes).
+static bool q_split_in_kernel(int64_t hd) { return hd == 256; }
 
 size_t eb_attn_prefill_workspace_bytes(int64_t h, int64_t hkv, int64_t s, int64_t hd) {
   if (!prefill_tc_supported((int)hd) || s <= 0 || hkv <= 0 || h <= 0) return 0;
-  return kv_split_bytes(s, hkv, hd) + q_prep_bytes(s, h, hd, true);
+  return kv_split_bytes(s, hkv, hd) + (q_split_in_kernel(hd) ? 0 : q_prep_bytes(s, h, hd, true));
 }
 
 int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, int64_t h,
@@ -418,8 +421,12 @@ int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, in
     pa.batch = 1;
     cudaError_t e = launch_prep_kv(pa, st);
     if (e != cudaSuccess) return cuda_status(e);
-    // q rows -> f16 hi/lo planes (k-only prep: no norm, no RoPE here)
-    void* qplanes = static_cast<char*>(workspace) + kv_split_bytes(s, hkv, hd);
+    // q rows -> f16 hi/lo planes (k-only prep: no norm, no RoPE here), or
+    // at head_dim 256 split inside the attention kernel
+    const bool qk = q_split_in_kernel(hd);
+    void* qplanes = qk ? const_cast<float*>(q)
+                       : static_cast<void*>(static_cast<char*>(workspace) +
+                                            kv_split_bytes(s, hkv, hd));
     PrepArgs qa{};
     qa.k = q;
     qa.dtype_kv = kF32;
@@ -430,12 +437,16 @@ int eb_attn_prefill(const float* q, const float* k, const float* v, float* o, in
     qa.hkv = (int)h;
     qa.hd = (int)hd;
     qa.batch = 1;
-    e = launch_prep_kv(qa, st);
-    if (e != cudaSuccess) return cuda_status(e);
+    if (!qk) {
+      e = launch_prep_kv(qa, st);
+      if (e != cudaSuccess) return cuda_status(e);
+    }
     PrefillArgs a{};
     a.o = o;
     a.dtype_o = kF32;
     a.o_stride = h * hd;
+    a.q_stride = h * hd;
+    a.q_dtype = kF32;
     a.S = (int)s;
     a.H = (int)h;
     a.Hkv = (int)hkv;
@@ -578,6 +589,10 @@ int eb_rope_tables(float* cos_t, float* sin_t, int64_t max_seq, int64_t head_dim
 static bool q_fused_path(const eb_attn_desc* d) {
   return d->dtype_cache != EB_F32 && d->dtype_qkv == d->dtype_cache;
 }
+// f32 caches at head_dim 256: the kernel reads q in any dtype and splits it.
+static bool q_fused_split(const eb_attn_desc* d) {
+  return d->dtype_cache == EB_F32 && q_split_in_kernel(d->head_dim);
+}
 
 size_t eb_attention_prefill_workspace_bytes(const eb_attn_desc* d, int64_t seq) {
   if (!desc_ok(d) || seq <= 0) return 0;
@@ -585,7 +600,7 @@ size_t eb_attention_prefill_workspace_bytes(const eb_attn_desc* d, int64_t seq) 
   const bool split = d->dtype_cache == EB_F32;
   if (q_fused_path(d)) return 0;
   return (split ? kv_split_bytes(seq, d->n_kv_heads, d->head_dim) : 0) +
-         q_prep_bytes(seq, d->n_heads, d->head_dim, split);
+         (q_fused_split(d) ? 0 : q_prep_bytes(seq, d->n_heads, d->head_dim, split));
 }
 
 // Shared argument checks of the prefill entry points.
@@ -662,15 +677,16 @@ static int prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, int64_t
     if (!aligned16(q) || !aligned16(o) || !aligned16(kcache) || !aligned16(vcache) ||
         ((qs_of(d) * eq) & 15) || ((os_of(d) * eo) & 15))
       return EB_ERR_INVALID_ARGUMENT;
-    const bool fused = q_fused_path(d);
+    const bool fused = q_fused_path(d), fused_split = q_fused_split(d);
     // q -> RMSNorm(q_norm_w) -> RoPE -> the MMA operand type (or f16 hi/lo
     // planes), the same row transform the k rows get: inside the attention
-    // kernel when q already has the operand type, else a row pass into the
-    // workspace
-    void* qprep = fused ? const_cast<void*>(q)
-                        : static_cast<char*>(workspace) +
-                              (split ? kv_split_bytes(seq, d->n_kv_heads, hd) : 0);
-    if (!fused) {
+    // kernel when q already has the operand type or the cache is f32 at
+    // head_dim 256, else a row pass into the workspace
+    void* qprep = (fused || fused_split)
+                      ? const_cast<void*>(q)
+                      : static_cast<char*>(workspace) +
+                            (split ? kv_split_bytes(seq, d->n_kv_heads, hd) : 0);
+    if (!fused && !fused_split) {
       PrepArgs qa{};
       qa.k = q;
       qa.dtype_kv = d->dtype_qkv;
@@ -695,6 +711,7 @@ static int prefill_attend(const eb_attn_desc* d, const eb_attn_layer* L, int64_t
     a.o_stride = os_of(d);
     a.q_fused = fused ? 1 : 0;
     a.q_stride = qs_of(d);
+    a.q_dtype = d->dtype_qkv;
     a.q_norm_w = L ? L->q_norm_w : nullptr;
     a.cos_t = cos_t;
     a.sin_t = sin_t;

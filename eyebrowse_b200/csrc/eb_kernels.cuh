@@ -204,9 +204,11 @@ struct PrefillArgs {
   const float* cos_t;
   const float* sin_t;
   float eps;
-  // f32 caches at head_dim 256: the f16 hi plane of the prepared query rows
-  // [S][H][hd], which the softmax threads copy into tensor memory.
-  const __half* q_hi;
+  // f32 caches at head_dim 256: the raw query rows [S][H][hd] (q_dtype,
+  // rows q_stride elements apart), which the softmax threads normalise,
+  // rotate and split into tensor memory (hi) and shared memory (lo).
+  const void* q_raw;
+  int q_dtype;
 };
 // Destinations of a head gather: up to kMaxGather buffers [S][H_total][hd]
 // in the output dtype (this GPU's and its peers', mapped here).

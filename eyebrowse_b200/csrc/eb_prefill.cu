@@ -124,39 +124,149 @@ struct GatherMaps {
 // as they are. Then the
 // generic-proxy writes are made visible to the tensor core and the tile's
 // ready barrier (128 arrivals) is arrived on.
-// Q in tensor memory (f32 caches at head_dim 256): thread r of the softmax
-// warpgroup copies its query row's f16 hi plane (HD values, already
-// normalised, rotated and split by the row-prep pass) into its TMEM lane,
-// element k at column k/2 of the given base, low half first -- the layout
-// of an A operand read from tensor memory (the same as P's). Rows past S
-// store zeros. The stores are warp-collective, so every thread makes them.
-// Then the tile's ready barrier (128 arrivals) tells the MMA thread.
+// Q in tensor memory (f32 caches at head_dim 256), with the q row prep
+// fused: thread r of the softmax warpgroup reads its raw query row (q_raw,
+// in dtype q_dtype, rows q_stride elements apart) from global memory and
+// applies the row-prep pass's per-element f32 arithmetic: RMSNorm with the
+// sum of squares in one thread's order (the reference's loop order,
+// crates/eyebrowse-kernels/src/rmsnorm.rs:34-36), then half-split RoPE at
+// position q_row (rope.rs:25-30), then the f16 hi/lo split. The hi plane
+// goes to its TMEM lane, element k at column k/2 of the given base, low
+// half first -- the layout of an A operand read from tensor memory (the
+// same as P's); the lo plane goes to the shared-memory tile (128-byte
+// swizzled boxes of [128 rows x 64 dims]) the QlKh MMAs read. Rows past S
+// store zeros. The TMEM stores are warp-collective, so every thread makes
+// them. Then the tile's ready barrier (128 arrivals) tells the MMA thread.
 template <int HD>
-__device__ __forceinline__ void q_hi_to_tmem(const PrefillArgs& a, uint32_t taddr, int q_row,
-                                             int h, bool valid, uint32_t ready_bar) {
-  const uint4* src =
-      reinterpret_cast<const uint4*>(a.q_hi + ((int64_t)(valid ? q_row : 0) * a.H + h) * HD);
+__device__ __forceinline__ void q_split_transform(const PrefillArgs& a, uint32_t taddr,
+                                                  uint32_t lo_tile, int r, int q_row, int h,
+                                                  bool valid, uint32_t ready_bar) {
+  constexpr int HALF = HD / 2, NCH = HD / 8;  // 8-element chunks per row
+  const bool rope = valid && a.cos_t != nullptr;
+  const bool norm = valid && a.q_norm_w != nullptr;
+  const int64_t base = (int64_t)(valid ? q_row : 0) * a.q_stride + (int64_t)h * HD;
+  // N chunks starting at c0 (stride cs chunks), as f32: every load of the
+  // batch is issued before any is used (the row is strided across the warp,
+  // so each batch is one round trip to memory).
+  auto load_chunks = [&](auto& f, int c0, int cs) {
+    constexpr int N = sizeof(f) / sizeof(f[0]);
+    if (!valid) {
 #pragma unroll
-  for (int half = 0; half < HD / 128; half++) {
-    // 128 values = 16 loads in flight, then two 32-column stores
-    uint4 x[16];
+      for (int n = 0; n < N; n++)
 #pragma unroll
-    for (int i = 0; i < 16; i++)
-      x[i] = valid ? __ldg(src + half * 16 + i) : make_uint4(0, 0, 0, 0);
+        for (int e = 0; e < 8; e++) f[n][e] = 0.f;
+    } else if (a.q_dtype == kF32) {
+      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.q_raw) + base);
+      float4 x[2 * N];
 #pragma unroll
-    for (int c = 0; c < 2; c++) {
-      uint32_t w[32];
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        w[4 * i] = x[c * 8 + i].x;
-        w[4 * i + 1] = x[c * 8 + i].y;
-        w[4 * i + 2] = x[c * 8 + i].z;
-        w[4 * i + 3] = x[c * 8 + i].w;
+      for (int n = 0; n < N; n++) {
+        x[2 * n] = __ldg(p + 2 * (c0 + n * cs));
+        x[2 * n + 1] = __ldg(p + 2 * (c0 + n * cs) + 1);
       }
-      tmem_st32(taddr + half * 64 + c * 32, w);
+#pragma unroll
+      for (int n = 0; n < N; n++) {
+        f[n][0] = x[2 * n].x; f[n][1] = x[2 * n].y; f[n][2] = x[2 * n].z; f[n][3] = x[2 * n].w;
+        f[n][4] = x[2 * n + 1].x; f[n][5] = x[2 * n + 1].y;
+        f[n][6] = x[2 * n + 1].z; f[n][7] = x[2 * n + 1].w;
+      }
+    } else {
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.q_raw) + base);
+      uint4 w[N];
+#pragma unroll
+      for (int n = 0; n < N; n++) w[n] = __ldg(p + c0 + n * cs);
+#pragma unroll
+      for (int n = 0; n < N; n++) {
+        const uint32_t u[4] = {w[n].x, w[n].y, w[n].z, w[n].w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const float2 v = a.q_dtype == kBF16
+                               ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[k]))
+                               : __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
+          f[n][2 * k] = v.x;
+          f[n][2 * k + 1] = v.y;
+        }
+      }
+    }
+  };
+  // hi of chunk c -> TMEM columns [4c, 4c+4), lo -> its swizzled shared-memory slot
+  auto put = [&](int c, const float (&x)[8]) {
+    uint32_t hw[4];
+    float lo[8];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const __half2 hh = __floats2half2_rn(x[2 * k], x[2 * k + 1]);
+      const float2 hf = __half22float2(hh);
+      hw[k] = *reinterpret_cast<const uint32_t*>(&hh);
+      lo[2 * k] = x[2 * k] - hf.x;
+      lo[2 * k + 1] = x[2 * k + 1] - hf.y;
+    }
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr + 4 * c),
+                 "r"(hw[0]), "r"(hw[1]), "r"(hw[2]), "r"(hw[3])
+                 : "memory");
+    st_chunk<false>(lo_tile + (uint32_t)(c >> 3) * (128u * 128u) +
+                        sw128_offset((uint32_t)r, (uint32_t)(c & 7)),
+                    lo);
+  };
+  float inv = 1.f;
+  if (norm) {
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < NCH; c0 += 16) {  // elements in order: one thread's sum
+      float f[16][8];
+      load_chunks(f, c0, 1);
+#pragma unroll
+      for (int n = 0; n < 16; n++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss = __fadd_rn(ss, __fmul_rn(f[n][e], f[n][e]));
+    }
+    inv = 1.0f / sqrtf(ss / (float)HD + a.eps);
+  }
+  const float* crow = rope ? a.cos_t + (int64_t)q_row * HALF : nullptr;
+  const float* srow = rope ? a.sin_t + (int64_t)q_row * HALF : nullptr;
+  constexpr int PB = 4;  // chunk pairs per batch
+#pragma unroll 1
+  for (int c0 = 0; c0 < NCH / 2; c0 += PB) {  // chunks c (first half) with partners c + NCH/2
+    float x[2 * PB][8];
+    load_chunks(*reinterpret_cast<float(*)[PB][8]>(&x[0]), c0, 1);
+    load_chunks(*reinterpret_cast<float(*)[PB][8]>(&x[PB]), c0 + NCH / 2, 1);
+    float4 tc[2 * PB], ts[2 * PB];
+    if (rope) {
+#pragma unroll
+      for (int i = 0; i < 2 * PB; i++) {
+        tc[i] = __ldg(reinterpret_cast<const float4*>(crow + 8 * c0) + i);
+        ts[i] = __ldg(reinterpret_cast<const float4*>(srow + 8 * c0) + i);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < PB; n++) {
+      const int c = c0 + n;
+      float* x1 = x[n];
+      float* x2 = x[PB + n];
+      if (norm) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          x1[e] = __fmul_rn(__fmul_rn(x1[e], inv), a.q_norm_w[8 * c + e]);
+          x2[e] = __fmul_rn(__fmul_rn(x2[e], inv), a.q_norm_w[HALF + 8 * c + e]);
+        }
+      }
+      if (rope) {
+        const float cs[8] = {tc[2 * n].x, tc[2 * n].y, tc[2 * n].z, tc[2 * n].w,
+                             tc[2 * n + 1].x, tc[2 * n + 1].y, tc[2 * n + 1].z, tc[2 * n + 1].w};
+        const float sn[8] = {ts[2 * n].x, ts[2 * n].y, ts[2 * n].z, ts[2 * n].w,
+                             ts[2 * n + 1].x, ts[2 * n + 1].y, ts[2 * n + 1].z, ts[2 * n + 1].w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float u = x1[e], v = x2[e];
+          x1[e] = __fsub_rn(__fmul_rn(u, cs[e]), __fmul_rn(v, sn[e]));
+          x2[e] = __fadd_rn(__fmul_rn(v, cs[e]), __fmul_rn(u, sn[e]));
+        }
+      }
+      put(c, x[n]);
+      put(c + NCH / 2, x[PB + n]);
     }
   }
   tmem_st_wait();
+  fence_async_smem();
   tc_fence_before();
   mbar_arrive(ready_bar);
 }
@@ -340,7 +450,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     // would put a load latency on every tile).
     if (lane == 0) {
       const bool is_k = warp == 0;
-      if (is_k) {
+      if (is_k && !C::QT) {  // QT: the softmax threads build the query tile
         // The query tiles (rows past S read as zeros): NQ heads x HB boxes of
         // [128 rows x 64 dims], hi and lo planes when split.
         mbar_arrive_expect_tx(bar(kBarQ), C::Q_BYTES);
@@ -349,14 +459,9 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
 #pragma unroll
           for (int hb = 0; hb < C::HB; hb++) {
             const uint32_t dst = sQ + t * C::QT_BYTES + hb * C::TILE128;
-            if constexpr (C::QT) {  // lo plane only: the hi plane goes to TMEM
-              tma_load_3d(dst, &tmQlo, bar(kBarQ), hb * 64, grp * NQ + t, q0);
-            } else {
-              tma_load_3d(dst, &tmQ, bar(kBarQ), hb * 64, grp * NQ + t, q0);
-              if (SPLIT)
-                tma_load_3d(dst + C::HB * C::TILE128, &tmQlo, bar(kBarQ), hb * 64, grp * NQ + t,
-                            q0);
-            }
+            tma_load_3d(dst, &tmQ, bar(kBarQ), hb * 64, grp * NQ + t, q0);
+            if (SPLIT)
+              tma_load_3d(dst + C::HB * C::TILE128, &tmQlo, bar(kBarQ), hb * 64, grp * NQ + t, q0);
           }
       }
       const int NST = is_k ? NSTK : NSTV;
@@ -382,7 +487,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         iss[sl]++;
       }
       // Every issued copy has landed before the CTA can exit.
-      if (is_k) mbar_drain(bar(kBarQ), 0, a.err, err_bit);
+      if (is_k && !C::QT) mbar_drain(bar(kBarQ), 0, a.err, err_bit);
       for (int s = 0; s < NST; s++)
         if (iss[s]) mbar_drain(bar(full0 + s), (iss[s] - 1) & 1, a.err, err_bit);
     }
@@ -445,7 +550,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
       };
       // The query tiles: landed (TMA), or landed and then transformed in
       // shared memory by their softmax warpgroups (fused q prep).
-      bool ok = a.q_fused ? true : mbar_wait(bar(kBarQ), 0, abort_flag, a.err, kErrTimeoutMma);
+      bool ok = (a.q_fused || C::QT) ? true
+                                     : mbar_wait(bar(kBarQ), 0, abort_flag, a.err, kErrTimeoutMma);
       if (ok && mbar_wait(bar(kKFull0), 0, abort_flag, a.err, kErrTimeoutMma)) {
 #pragma unroll
         for (int t = 0; t < NQ; t++) {
@@ -546,8 +652,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     const uint32_t tO = tmem + lane_off + t * HD;
     if (a.q_fused) q_tile_transform<HD, BF16>(sQ + t * C::QT_BYTES, r, q_row, a, bar(kBarQ),
                                              bar(kQReady0 + t), abort_flag);
-    if constexpr (C::QT) q_hi_to_tmem<HD>(a, tmem + lane_off + C::Q_TM, q_row, h, valid,
-                                          bar(kQReady0 + t));
+    if constexpr (C::QT) q_split_transform<HD>(a, tmem + lane_off + C::Q_TM, sQ + t * C::QT_BYTES,
+                                               r, q_row, h, valid, bar(kQReady0 + t));
     // With a window the running max starts finite: a row can see no key of
     // its first tiles (S row all -inf), and -inf - (-inf) would turn its P
     // into NaN. Any finite score later rescales by ex2(-1e30 - m) = 0.
@@ -895,13 +1001,13 @@ static cudaError_t run_prefill_k(const PrefillArgs& a, const void* q16, const vo
     __atomic_fetch_or(&configured, 1u << (dev & 31), __ATOMIC_RELEASE);
   }
   CUtensorMap mq, mql, mk, mv, mkl, mvl;
-  const __half* ka_q_hi = nullptr;
-  if (SPLIT) {
+  if (SPLIT && !PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::QT) {
     const __half* qp = reinterpret_cast<const __half*>(q16);
-    ka_q_hi = qp;
     if (!make_kv_map(&mq, qp, a.S, a.H, HD, 128, false) ||
         !make_kv_map(&mql, qp + (size_t)a.S * a.H * HD, a.S, a.H, HD, 128, false))
       return cudaErrorInvalidValue;
+  } else if (C::QT) {
+    // the kernel reads the raw q rows itself (q_raw): no query tensor map
   } else if (a.q_fused) {
     if (!make_q_map(&mq, q16, a.S, a.H, HD, a.q_stride, BF16)) return cudaErrorInvalidValue;
     mql = mq;
@@ -928,7 +1034,12 @@ static cudaError_t run_prefill_k(const PrefillArgs& a, const void* q16, const vo
   memset(&gm, 0, sizeof(gm));
   PrefillArgs ka = a;
   ka.n_dst = 0;
-  ka.q_hi = ka_q_hi;
+  if (C::QT) {
+    // unused by this kernel; any valid map fills the parameter slots
+    mq = mk;
+    mql = mk;
+    ka.q_raw = q16;
+  }
   if (g && g->n_dst > 0) {
     if (g->n_dst > kMaxGather) return cudaErrorInvalidValue;
     for (int d = 0; d < g->n_dst; d++)
