@@ -209,6 +209,8 @@ struct PrefillArgs {
   // rotate and split into tensor memory (hi) and shared memory (lo).
   const void* q_raw;
   int q_dtype;
+  // set by the launcher: the RoPE table rows come by TMA (tmCos / tmSin)
+  int tab_smem;
 };
 // Destinations of a head gather: up to kMaxGather buffers [S][H_total][hd]
 // in the output dtype (this GPU's and its peers', mapped here).

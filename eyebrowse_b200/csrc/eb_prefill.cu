@@ -77,6 +77,16 @@ struct PfCfg {
   static constexpr int V_OFF = Q_BYTES + NSTK * K_BYTES;  // V ring follows the K ring
   static constexpr int BAR_OFF = V_OFF + NSTV * K_BYTES;
   static constexpr int SMEM = BAR_OFF + 512 + 1024;  // barriers/flags + alignment slack
+  // Fused q prep with RoPE: the CTA's 128 rows of the cos / sin tables
+  // (HD/2 f32 each) come by TMA with the query tiles, as [128 rows x 128 B]
+  // 128-byte-swizzled boxes, into the last K slot (cos) and the last V slot
+  // (sin). Those slots take their first K/V tiles once every query tile's
+  // rows are transformed. (Per-thread loads of a table row each touch 32
+  // cache lines per warp instruction and took ~2 us per batch at CTA start.)
+  static constexpr int TAB_BYTES = 128 * (HD / 2) * 4;
+  static constexpr bool TAB = !SPLIT && NSTK >= 2 && NSTV >= 2 && TAB_BYTES <= K_BYTES;
+  static constexpr int TAB_COS = Q_BYTES + (NSTK - 1) * K_BYTES;  // offsets from the tile base
+  static constexpr int TAB_SIN = V_OFF + (NSTV - 1) * K_BYTES;
   static constexpr int NSB = (NQ == 1 || NQ * HD + NQ * 2 * BN <= 512) ? 2 : 1;
   // TMEM columns: the O accumulators first ([t*HD, (t+1)*HD)), then Q's hi
   // plane when QT (HD/2 columns of packed f16 pairs), then the S/P buffers;
@@ -274,7 +284,8 @@ __device__ __forceinline__ void q_split_transform(const PrefillArgs& a, uint32_t
 template <int HD, bool BF16>
 __device__ __forceinline__ void q_tile_transform(uint32_t tile, int r, int q_row,
                                                  const PrefillArgs& a, uint32_t q_bar,
-                                                 uint32_t ready_bar, volatile int* abort_flag) {
+                                                 uint32_t ready_bar, volatile int* abort_flag,
+                                                 uint32_t tab_cos, uint32_t tab_sin) {
   constexpr int HALF = HD / 2, NCH = HD / 8;  // 8-element chunks per row
   const bool valid = q_row < a.S;
   const bool rope = valid && a.cos_t != nullptr;
@@ -302,19 +313,32 @@ __device__ __forceinline__ void q_tile_transform(uint32_t tile, int r, int q_row
   constexpr int PP = HALF < 32 ? HALF : 32;  // pairs per pass
   constexpr int NPASS = HALF / PP;
   float cs[PP], sn[PP];
+  // tab_cos != 0: the table rows are staged in shared memory (128-byte
+  // swizzled boxes of 32 pairs x 128 rows, landed with the query tile)
+  auto lds4 = [&](uint32_t base, int i) {  // pairs i..i+3 of row r
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(base + (uint32_t)(i >> 5) * (128u * 128u) +
+                       sw128_offset((uint32_t)r, (uint32_t)((i & 31) >> 2))));
+    return v;
+  };
   auto fetch = [&](int pass) {
 #pragma unroll
     for (int i = 0; i < PP; i += 4) {
-      const float4 c4 = rope ? *reinterpret_cast<const float4*>(crow + pass * PP + i)
-                             : make_float4(1.f, 1.f, 1.f, 1.f);
-      const float4 s4 = rope ? *reinterpret_cast<const float4*>(srow + pass * PP + i)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 c4 = !rope ? make_float4(1.f, 1.f, 1.f, 1.f)
+                        : tab_cos ? lds4(tab_cos, pass * PP + i)
+                                  : *reinterpret_cast<const float4*>(crow + pass * PP + i);
+      const float4 s4 = !rope ? make_float4(0.f, 0.f, 0.f, 0.f)
+                        : tab_cos ? lds4(tab_sin, pass * PP + i)
+                                  : *reinterpret_cast<const float4*>(srow + pass * PP + i);
       cs[i] = c4.x; cs[i + 1] = c4.y; cs[i + 2] = c4.z; cs[i + 3] = c4.w;
       sn[i] = s4.x; sn[i + 1] = s4.y; sn[i + 2] = s4.z; sn[i + 3] = s4.w;
     }
   };
-  if (rope) fetch(0);
+  if (rope && !tab_cos) fetch(0);  // global rows: in flight while the tile lands
   const bool got_q = mbar_wait(q_bar, 0, abort_flag, a.err, kErrTimeoutSoftmax);
+  if (rope && tab_cos && got_q) fetch(0);
   if (got_q && (rope || norm)) {
     float inv = 1.f;
     if (norm) {
@@ -372,6 +396,8 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
                       const __grid_constant__ CUtensorMap tmV,
                       const __grid_constant__ CUtensorMap tmKlo,
                       const __grid_constant__ CUtensorMap tmVlo,
+                      const __grid_constant__ CUtensorMap tmCos,
+                      const __grid_constant__ CUtensorMap tmSin,
                       const __grid_constant__ GatherMaps gmaps, PrefillArgs a) {
   using C = PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>;
   constexpr int NSB = C::NSB;
@@ -439,6 +465,7 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const bool tab = C::TAB && a.tab_smem != 0;
 
   if (warp == 0 || warp == 2) {
     // ------------------------------------------------------------ TMA producers
@@ -452,8 +479,16 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
       const bool is_k = warp == 0;
       if (is_k && !C::QT) {  // QT: the softmax threads build the query tile
         // The query tiles (rows past S read as zeros): NQ heads x HB boxes of
-        // [128 rows x 64 dims], hi and lo planes when split.
-        mbar_arrive_expect_tx(bar(kBarQ), C::Q_BYTES);
+        // [128 rows x 64 dims], hi and lo planes when split. With staged RoPE
+        // tables, their rows come on the same barrier.
+        mbar_arrive_expect_tx(bar(kBarQ), C::Q_BYTES + (tab ? 2 * C::TAB_BYTES : 0));
+        if (tab) {
+#pragma unroll
+          for (int bx = 0; bx < HD / 64; bx++) {  // boxes of 32 pairs
+            tma_load_2d(sQ + C::TAB_COS + bx * C::TILE128, &tmCos, bar(kBarQ), bx * 32, q0);
+            tma_load_2d(sQ + C::TAB_SIN + bx * C::TILE128, &tmSin, bar(kBarQ), bx * 32, q0);
+          }
+        }
 #pragma unroll
         for (int t = 0; t < NQ; t++)
 #pragma unroll
@@ -477,6 +512,13 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
         const uint32_t dst = ring + sl * C::K_BYTES;
         if (j >= NST && !mbar_wait(bar(empty0 + sl), (j / NST - 1) & 1, abort_flag, a.err, err_bit))
           break;
+        if (tab && j == NST - 1) {  // the slot holds a staged table until the q rows are done
+          bool got = true;
+#pragma unroll
+          for (int t = 0; t < NQ; t++)
+            got = got && mbar_wait(bar(kQReady0 + t), 0, abort_flag, a.err, err_bit);
+          if (!got) break;
+        }
         const uint32_t fb = bar(full0 + sl);
         mbar_arrive_expect_tx(fb, C::K_BYTES);
 #pragma unroll
@@ -650,8 +692,9 @@ __global__ void __launch_bounds__(PfCfg<HD, BN, NQ, SPLIT, NSTK, NSTV>::THREADS,
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const float sl2 = a.scale_log2;
     const uint32_t tO = tmem + lane_off + t * HD;
-    if (a.q_fused) q_tile_transform<HD, BF16>(sQ + t * C::QT_BYTES, r, q_row, a, bar(kBarQ),
-                                             bar(kQReady0 + t), abort_flag);
+    if (a.q_fused)
+      q_tile_transform<HD, BF16>(sQ + t * C::QT_BYTES, r, q_row, a, bar(kBarQ), bar(kQReady0 + t),
+                                 abort_flag, tab ? sQ + C::TAB_COS : 0u, sQ + C::TAB_SIN);
     if constexpr (C::QT) q_split_transform<HD>(a, tmem + lane_off + C::Q_TM, sQ + t * C::QT_BYTES,
                                                r, q_row, h, valid, bar(kQReady0 + t));
     // With a window the running max starts finite: a row can see no key of
@@ -966,6 +1009,20 @@ static bool make_q_map(CUtensorMap* m, const void* base, int S, int H, int hd,
   return r == CUDA_SUCCESS;
 }
 
+// 2-D map over a RoPE table [rows][half] f32, box {32, 128}, 128-byte swizzle.
+static bool make_table_map(CUtensorMap* m, const float* base, int rows, int half) {
+  auto fn = encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)half, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)half * 4};
+  cuuint32_t box[2] = {32, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // 3-D map over a gathered output [S][H_total][hd] of dtype dt (16-bit or
 // f32), box {128 bytes of one head row, 1 head, 128 rows}, 128-byte swizzle.
 static bool make_out_map(CUtensorMap* m, uint64_t base, int S, int64_t h_total, int hd, int dt) {
@@ -1049,7 +1106,16 @@ static cudaError_t run_prefill_k(const PrefillArgs& a, const void* q16, const vo
     ka.h_off = g->h_off;
   }
   const int n_qt = (a.S + 127) / 128;
-  kern<<<(unsigned)(n_qt * (a.H / NQ)), C::THREADS, C::SMEM, st>>>(mq, mql, mk, mv, mkl, mvl, gm,
+  // staged RoPE table rows (fused q prep): 2-D maps over cos / sin [S][HD/2]
+  // f32, box {32 pairs, 128 rows}; without them the kernel reads the rows
+  // from global memory
+  CUtensorMap mcos = mk, msin = mk;
+  ka.tab_smem = 0;
+  if (C::TAB && a.q_fused && a.cos_t && a.sin_t && make_table_map(&mcos, a.cos_t, a.S, HD / 2) &&
+      make_table_map(&msin, a.sin_t, a.S, HD / 2))
+    ka.tab_smem = 1;
+  kern<<<(unsigned)(n_qt * (a.H / NQ)), C::THREADS, C::SMEM, st>>>(mq, mql, mk, mv, mkl, mvl, mcos,
+                                                                     msin, gm,
                                                                      ka);
   return cudaGetLastError();
 }
