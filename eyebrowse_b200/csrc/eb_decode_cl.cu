@@ -14,10 +14,12 @@
 //     the new row's cache write) runs while they are in flight;
 //   - with 8 warps per CTA and at most 16 CTAs per (sequence, group), a
 //     CTA's chunk is mostly one batch;
-//   - the partials never leave the cluster: after a cluster barrier, rank 0
-//     reads every CTA's (m, l, O) from its shared memory and writes o.
+//   - the partials never leave the cluster: every CTA stores its (m, l, O)
+//     into rank 0's shared memory (distributed shared memory), and after one
+//     cluster barrier rank 0 combines them locally and writes o while the
+//     other CTAs exit.
 // Grid (chunks, kv-head groups, sequences), cluster (chunks, 1, 1): cluster
-// rank == chunk. Every CTA reaches both cluster barriers (CTAs past a short
+// rank == chunk. Every CTA reaches the cluster barrier (CTAs past a short
 // sequence's context contribute an empty partial).
 #include <cooperative_groups.h>
 
@@ -52,9 +54,10 @@ struct ClShape {
   static constexpr int NS = kClWarps * RPW;                 // softmax slots per CTA
   static constexpr int U = cl_steps(G, LOADS, EPL);
   static constexpr int RPB = kClWarps * RPW * U;            // rows per CTA batch
-  // dynamic shared memory: slot accumulators, then the CTA's merged partial
+  // dynamic shared memory: slot accumulators, then the partials of the n
+  // chunks of the cluster (every CTA pushes its own into rank 0's copy)
   static constexpr int SACC = NS * G * HD;
-  static constexpr int SMEM = (SACC + G * HD) * 4;
+  static constexpr int smem(int n) { return (SACC + n * G * HD) * 4; }
 };
 
 int decode_cl_rows_per_batch(int hd, int dtype_cache, int group) {
@@ -85,10 +88,11 @@ __global__ void __launch_bounds__(kClWarps * 32, 1) decode_cl_kernel(DecodeArgs 
   constexpr int NS = Sh::NS, U = Sh::U;
   extern __shared__ __align__(16) float dyn[];
   float* sacc = dyn;                 // [NS][G][HD]
-  float* part_acc = dyn + Sh::SACC;  // [G][HD]: this CTA's merged partial
+  float* recv_acc = dyn + Sh::SACC;  // [n][G][HD]: rank 0's copy receives every chunk's O
   __shared__ __align__(16) float qs[G][HD];
   __shared__ float sm_m[NS][G], sm_l[NS][G];
   __shared__ float part_m[G], part_l[G];
+  __shared__ float recv_m[kClMaxChunks][G], recv_l[kClMaxChunks][G];
 
   cg::cluster_group cluster = cg::this_cluster();
   const int c = blockIdx.x;    // chunk == cluster rank
@@ -302,6 +306,8 @@ __global__ void __launch_bounds__(kClWarps * 32, 1) decode_cl_kernel(DecodeArgs 
         if (sm_m[s2][tid] != -INFINITY) L += sm_l[s2][tid] * ex2(sm_m[s2][tid] - M);
     part_m[tid] = M;
     part_l[tid] = L;
+    *cluster.map_shared_rank(&recv_m[c][tid], 0) = M;
+    *cluster.map_shared_rank(&recv_l[c][tid], 0) = L;
   }
   __syncthreads();
   for (int idx = tid; idx < G * HD; idx += kClWarps * 32) {
@@ -311,43 +317,28 @@ __global__ void __launch_bounds__(kClWarps * 32, 1) decode_cl_kernel(DecodeArgs 
     if (M != -INFINITY)
       for (int s2 = 0; s2 < NS; s2++)
         if (sm_m[s2][g] != -INFINITY) O += sacc[(s2 * G + g) * HD + d] * ex2(sm_m[s2][g] - M);
-    part_acc[idx] = O;
+    *cluster.map_shared_rank(&recv_acc[c * G * HD + idx], 0) = O;  // into rank 0
   }
 
-  // ---- combine across the cluster: rank 0 reads every CTA's partial
-  cluster.sync();  // every partial written (release), visible to the cluster (acquire)
+  // ---- combine across the cluster: every chunk's partial is in rank 0's
+  // shared memory once the barrier completes (release/acquire); the other
+  // CTAs are done and may exit, rank 0 combines from local memory.
+  cluster.sync();
   if (c == 0) {
-    // every remote load of an element issued at once (one trip, not 3n)
     const int n = (int)gridDim.x;
     for (int idx = tid; idx < G * HD; idx += kClWarps * 32) {
       const int g = idx / HD, d = idx % HD;
-      float mv[kClMaxChunks], lv[kClMaxChunks], av[kClMaxChunks];
-#pragma unroll
-      for (int cc = 0; cc < kClMaxChunks; cc++) {
-        if (cc < n) {
-          mv[cc] = *cluster.map_shared_rank(&part_m[g], cc);
-          lv[cc] = *cluster.map_shared_rank(&part_l[g], cc);
-          av[cc] = *cluster.map_shared_rank(&part_acc[idx], cc);
-        } else {
-          mv[cc] = -INFINITY;
-          lv[cc] = 0.f;
-          av[cc] = 0.f;
-        }
-      }
       float M = -INFINITY;
-#pragma unroll
-      for (int cc = 0; cc < kClMaxChunks; cc++) M = fmaxf(M, mv[cc]);
+      for (int cc = 0; cc < n; cc++) M = fmaxf(M, recv_m[cc][g]);
       float L = 0.f, O = 0.f;
-#pragma unroll
-      for (int cc = 0; cc < kClMaxChunks; cc++) {
-        const float w = mv[cc] == -INFINITY ? 0.f : ex2(mv[cc] - M);
-        L += lv[cc] * w;
-        O += av[cc] * w;
+      for (int cc = 0; cc < n; cc++) {
+        const float w = recv_m[cc][g] == -INFINITY ? 0.f : ex2(recv_m[cc][g] - M);
+        L += recv_l[cc][g] * w;
+        O += recv_acc[cc * G * HD + idx] * w;
       }
       dec_store(a, b, head0 + g, HD, d, O / L);
     }
   }
-  cluster.sync();  // no CTA leaves while rank 0 still reads its shared memory
 }
 
 template <int HD, typename TC>
@@ -375,10 +366,10 @@ static cudaError_t launch_cl_g(const DecodeArgs& a, int batch, int n_chunks, cud
     return cudaLaunchKernelEx(&cfg, kern, a, gsubs);
   };
   switch (gs) {
-    case 8: return go(decode_cl_kernel<HD, TC, 8>, ClShape<HD, TC, 8>::SMEM);
-    case 4: return go(decode_cl_kernel<HD, TC, 4>, ClShape<HD, TC, 4>::SMEM);
-    case 2: return go(decode_cl_kernel<HD, TC, 2>, ClShape<HD, TC, 2>::SMEM);
-    default: return go(decode_cl_kernel<HD, TC, 1>, ClShape<HD, TC, 1>::SMEM);
+    case 8: return go(decode_cl_kernel<HD, TC, 8>, ClShape<HD, TC, 8>::smem(n_chunks));
+    case 4: return go(decode_cl_kernel<HD, TC, 4>, ClShape<HD, TC, 4>::smem(n_chunks));
+    case 2: return go(decode_cl_kernel<HD, TC, 2>, ClShape<HD, TC, 2>::smem(n_chunks));
+    default: return go(decode_cl_kernel<HD, TC, 1>, ClShape<HD, TC, 1>::smem(n_chunks));
   }
 }
 
@@ -390,7 +381,7 @@ static int active_clusters(int n) {
   int v = __atomic_load_n(&cache[n], __ATOMIC_RELAXED);
   if (v > 0) return v - 1;
   auto kern = decode_cl_kernel<HD, TC, G>;
-  constexpr int smem = ClShape<HD, TC, G>::SMEM;
+  const int smem = ClShape<HD, TC, G>::smem(n);
   int num = 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)n, 1, 1);
