@@ -53,8 +53,11 @@ __global__ void __launch_bounds__(96)
   using TC = std::conditional_t<BF16, __nv_bfloat16, __half>;
   constexpr int E = HD / 32;
   // KV-head group fastest: the heads of one chunk share cache rows (and DRAM
-  // pages) and run side by side
-  const int grp = blockIdx.x, c = blockIdx.y, b = blockIdx.z;
+  // pages) and run side by side. Chunk index slowest: every sequence's first
+  // chunk is dispatched before any second chunk, so the last waves hold only
+  // the later chunks of the longest contexts, not whichever full chunks came
+  // last in sequence order (an idle tail of up to one full chunk per SM).
+  const int grp = blockIdx.x, b = blockIdx.y, c = blockIdx.z;
   const int G = a.H / a.Hkv / gsubs;  // query heads handled here (<= 32)
   const int kvh = grp / gsubs, sub = grp % gsubs;
   const int head0 = kvh * (G * gsubs) + sub * G;
@@ -509,7 +512,7 @@ static cudaError_t run_decode_tc(const DecodeArgs& a, int batch, int gsubs, cuda
   if (!make_cache_map(&mk, a.kcache, batch, a.max_seq, a.Hkv, HD, a.cache_bstride, BN, BF16) ||
       !make_cache_map(&mv, a.vcache, batch, a.max_seq, a.Hkv, HD, a.cache_bstride, BN, BF16))
     return cudaErrorInvalidValue;
-  dim3 grid(a.Hkv * gsubs, a.cmax, batch);
+  dim3 grid(a.Hkv * gsubs, batch, a.cmax);
   kern<<<grid, 96, C::SMEM, st>>>(mk, mv, a, gsubs);
   return cudaGetLastError();
 }
