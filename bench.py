@@ -68,15 +68,21 @@ KERNEL_SOURCES = {
 
 
 def source_hash(key: str):
-    """sha256 (first 16 hex digits) of the kernel sources behind `key`."""
+    """sha256 (first 16 hex digits) of the kernel sources behind `key`, with
+    comments and white space removed: a capture stays valid across comment
+    edits and goes stale with any change to the code."""
     import hashlib
+    import re
     names = KERNEL_SOURCES.get(key)
     if not names:
         return None
     h = hashlib.sha256()
     for n in names:
-        with open(os.path.join(ROOT, "eyebrowse_b200", "csrc", n), "rb") as f:
-            h.update(f.read())
+        with open(os.path.join(ROOT, "eyebrowse_b200", "csrc", n)) as f:
+            src = f.read()
+        src = re.sub(r"/\*.*?\*/", " ", src, flags=re.S)  # block comments
+        src = re.sub(r"//[^\n]*", " ", src)                # line comments
+        h.update("".join(src.split()).encode())
     return h.hexdigest()[:16]
 
 

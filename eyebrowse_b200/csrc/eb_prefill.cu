@@ -6,10 +6,11 @@
 //
 // One CTA = NQ query tiles of 128 rows (the two heads of a GQA pair when the
 // group size is even, so each K/V tile feeds twice the MMA work):
-//   warp 0      TMA producer: the query tiles (normalised, rotated and
-//               rounded by the row-prep pass, or the raw 16-bit rows the
-//               softmax warps transform in place), then K tiles [BN rows x 64
-//               dims] (128-byte swizzle) into an NSTK-deep ring.
+//   warp 0      TMA producer: the query tiles (the raw 16-bit rows the
+//               softmax warps transform in place, with the CTA's rows of the
+//               RoPE tables; or rows the row-prep pass already transformed),
+//               then K tiles [BN rows x 64 dims] (128-byte swizzle) into an
+//               NSTK-deep ring.
 //   warp 1      TMEM owner + MMA issuer (one thread): S_t = Q_t K^T into TMEM,
 //               then O_t += P_t V with P read from TMEM (it overwrites S_t).
 //   warp 2      TMA producer of the V ring (its own thread, so K loads never
@@ -20,7 +21,8 @@
 //               row from TMEM, online softmax in f32 (exp2 on MUFU, some
 //               column pairs on the FMA pipe), rescale the O row in TMEM when
 //               the max moves past a threshold, write P (16-bit) back over S;
-//               finally O / l to global memory.
+//               finally O / l to global memory. Before the first tile they
+//               normalise and rotate their query rows (fused q prep).
 // K/V come from the cache the K/V preparation pass has just written (the
 // reference attends the same post-RoPE k / post-norm v it writes,
 // crates/eyebrowse-nn/src/attention.rs:78-115).
@@ -34,7 +36,9 @@
 // values: o is then an exact convex combination of v rows whose weights are
 // each off by at most 2^-11 relative and still sum to one, so the error is
 // at most 2^-11 times the weighted spread of v about o (none when one key
-// carries all the weight).
+// carries all the weight). At head_dim 256 Q's hi plane sits in tensor
+// memory and the softmax threads build both planes from the raw q rows (see
+// PfCfg::QT and q_split_transform).
 #include <cudaTypedefs.h>
 
 #include <algorithm>
