@@ -36,3 +36,24 @@ def test_linear_units():
     w = bench.make_workload("projd")
     assert w.bound == "hbm"
     assert w.bytes_total() == 2.0 * 151936 * 1024 + 4.0 * (1024 + 151936)
+
+
+def test_profile_traffic_is_keyed_to_the_kernel_code(tmp_path, monkeypatch):
+    """A traffic[...] line counts only while the kernel code it was captured
+    from is unchanged: comment edits keep it, a code edit drops it (None)."""
+    csrc = tmp_path / "eyebrowse_b200" / "csrc"
+    csrc.mkdir(parents=True)
+    prof = tmp_path / "profiles"
+    prof.mkdir()
+    src = csrc / "k.cu"
+    src.write_text("// kernel\n__global__ void k(int* p) { p[0] = 1; }  /* note */\n")
+    monkeypatch.setattr(bench, "ROOT", str(tmp_path))
+    monkeypatch.setitem(bench.KERNEL_SOURCES, "toy", ("k.cu",))
+    h = bench.source_hash("toy")
+    (prof / "toy.md").write_text(f"traffic[toy]: 1234 bytes per launch, source {h}\n")
+    assert bench.profile_traffic("toy") == 1234.0
+    src.write_text("// the same kernel, re-commented\n__global__ void k(int* p) {\n  p[0] = 1;\n}\n")
+    assert bench.source_hash("toy") == h and bench.profile_traffic("toy") == 1234.0
+    src.write_text("__global__ void k(int* p) { p[0] = 2; }\n")
+    assert bench.source_hash("toy") != h and bench.profile_traffic("toy") is None
+    assert bench.rank_traffic("toy", 0.5) is None
