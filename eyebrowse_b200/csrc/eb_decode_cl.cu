@@ -196,6 +196,22 @@ __global__ void __launch_bounds__(kClWarps * 32, 1) decode_cl_kernel(DecodeArgs 
     }
   };
   load_batch(row_begin);
+  // The later batches' rows into L2 now (a hint: no registers, no waiting),
+  // so each load after the first batch finds them there instead of waiting
+  // on HBM behind the previous batch's compute.
+  for (int r1 = row_begin + Sh::RPB; r1 < row_end; r1 += Sh::RPB) {
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int row = r1 + (u * kClWarps + warp) * RPW + slot;
+      if (row < row_end) {
+#pragma unroll
+        for (int t = 0; t < LOADS; t++) {
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(kc + (int64_t)row * rstride + t * LPR * VEC));
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(vc + (int64_t)row * rstride + t * LPR * VEC));
+        }
+      }
+    }
+  }
   if (warp < n_jobs) job_math(warp, job);
   for (int j = warp + kClWarps; j < n_jobs; j += kClWarps) {  // G = 8 with a new row
     job_load(j, job);
