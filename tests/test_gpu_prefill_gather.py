@@ -9,7 +9,7 @@ at the north-star tolerance on the checked rows.
 Covers the one-tile kernel (a shard with few heads: the longest item
 decides the grid) and the two-tile GQA-pair kernel, 16-bit q with the q prep
 and its RoPE table rows fused into the kernel, a ragged last tile, and the
-shard shape of config 3 on 8 GPUs at its full length."""
+shard shapes of config 3 on 4 and 8 GPUs at full length."""
 import os
 
 import numpy as np
@@ -25,6 +25,7 @@ pytestmark = pytest.mark.gpu
     (4608, 32, 8, 2, "f16"),   # 16 heads per shard: GQA-pair kernel
     (1100, 16, 8, 2, "bf16"),  # 8 heads per shard, bf16
     (8192, 32, 8, 8, "f16"),   # config 3 over 8 GPUs: 4 heads, 1 KV head per shard
+    (8192, 32, 8, 4, "f16"),   # config 3 over 4 GPUs: 8 heads, 2 KV heads per shard
 ])
 def test_prefill_gather_assembles_the_full_output(eb, orc, S, H, Hkv, world, dt):
     import torch
