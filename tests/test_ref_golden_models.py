@@ -36,8 +36,9 @@ def test_fixture_came_from_the_reference_generator(name):
     where the reference checkout is present, it must be the current script."""
     z = np.load(_fixture(name))
     digest = bytes(z["__generator_sha256__"]).decode()
-    src = os.path.join(os.environ.get("EYEBROWSE_REF", "/root/reference"), "golden",
-                       SCRIPTS[name])
+    # the reference checkout: $EYEBROWSE_REF, else a "reference" folder beside this repository
+    ref = os.environ.get("EYEBROWSE_REF", os.path.join(os.path.dirname(ROOT), "reference"))
+    src = os.path.join(ref, "golden", SCRIPTS[name])
     if not os.path.exists(src):
         pytest.skip("reference checkout not present")
     with open(src, "rb") as f:
