@@ -1,15 +1,21 @@
 """Benchmark of the eyebrowse B200 attention path (BASELINE.json metric:
 "prefill attn TFLOP/s & decode KV GB/s at 1/2/4/8 B200 vs roofline").
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg3|cfg1|cfg2|cfg4|cfg5]
-                    [--impl ours|reference] [--no-decode] [--no-cpu]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload W]
+                    [--impl ours|reference] [--no-decode] [--no-cpu] [--gather fused|nccl]
+
+Workloads: cfg3 (default), cfg1, cfg2, cfg4, cfg4d (config 4's decode step),
+cfg5, cfg3w (config 3 with a sliding window), cfg3r4 / cfg3r8 (one rank's
+head share of config 3 at 4 / 8 GPUs, on one GPU without the gather), proj3,
+projd (projections).
 
 The headline line is config 3 (causal GQA prefill, S8192 H32 Hkv8 hd128, f16
 q/k/v/cache/out, f32 accumulate, RoPE theta 5e5), heads sharded over N ranks
 (strong scaling): each rank runs the fused prefill on its H/N query heads and
-Hkv/N KV heads, then NCCL all-gathers the per-rank outputs at the head-concat
-boundary and a concat kernel restores [S, H, hd]. A "step" is that whole
-sequence. `value` is total algorithmic FLOP / max-over-ranks step time.
+Hkv/N KV heads, and the attention kernel stores its output tiles into every
+rank's gathered [S, H, hd] buffer over NVLink (--gather nccl: an NCCL
+all-gather and a concat kernel instead). A "step" is that whole sequence.
+`value` is total algorithmic FLOP / max-over-ranks step time.
 The "decode" object is config 5 (64 sequences, contexts U[512, 32768], f16
 caches), sharded by KV head, in KV GB/s.
 
@@ -767,6 +773,11 @@ def make_workload(name, batch=None):
     if name == "cfg3w":
         return PrefillWork("cfg3w config 3 with a 1024-row sliding window (S8192 H32 Hkv8 hd128 "
                            "f16)", 8192, 32, 8, 128, 5e5, 1, in_scale=0.5, seed=3, window=1024)
+    if name in ("cfg3r4", "cfg3r8"):
+        g = 4 if name == "cfg3r4" else 8
+        return PrefillWork(f"{name} one rank's head share of config 3 at {g} GPUs, run on one GPU "
+                           f"without the gather: S8192 H{32 // g} Hkv{8 // g} hd128 f16",
+                           8192, 32 // g, 8 // g, 128, 5e5, 1, in_scale=0.5, seed=3)
     if name == "cfg4":
         return PrefillWork("cfg4 Gemma-style prefill S4096 H8 Hkv4 hd256 f32 scale 1.0 "
                            "QK-norm V-norm partial rotary 32/128", 4096, 8, 4, 256, 1e6, 0,
